@@ -1,0 +1,117 @@
+/*
+ * gemm_sm100.h -- C ABI of the B200 (sm_100a) FP16 GEMM kernel bank.
+ *
+ * C[M,N] (fp16) = A[M,K] (fp16) * B[K,N] (fp16), fp32 accumulation, all
+ * matrices row-major with element pitches lda / ldb / ldc.
+ *
+ * This library replaces the reference extension `infinite_dreams_ext`
+ * (src/gemm_ext.cpp:123-132) and its launcher chain
+ * (src/gemm_cuda.cu:5-15, generated gemm_try_bank_NNN from
+ * src/gen_gemm_bank.py:216-236).  Every entry point below names the
+ * reference interface it replaces.  The signatures carry plain pointers and
+ * sizes only; no torch types cross this boundary.
+ *
+ * Ownership: the caller owns A, B, C and the workspace.  gemm_launch is
+ * asynchronous on the caller's stream and allocates nothing.  Calls from
+ * several host threads are safe; launches that share one workspace must not
+ * overlap on the GPU.
+ *
+ * Errors: every entry point returns a status code (never fails silently; the
+ * reference launched nothing and returned an uninitialised tensor when a tile
+ * was not in its menu).  gemm_last_error() gives a message for the calling
+ * thread's most recent failure.
+ */
+#ifndef INFINITE_DREAMS_GEMM_SM100_H_
+#define INFINITE_DREAMS_GEMM_SM100_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define GEMM_OK 0
+#define GEMM_ERR_INVALID_ARG 1     /* bad sizes, pitches, null pointers       */
+#define GEMM_ERR_BAD_CFG 2         /* cfg_id / knob tuple not in the menu      */
+#define GEMM_ERR_WORKSPACE 3       /* workspace missing or too small           */
+#define GEMM_ERR_CUDA 4            /* a CUDA runtime / driver call failed      */
+#define GEMM_ERR_UNSUPPORTED 5     /* device is not sm_100 or shape too large  */
+#define GEMM_ERR_DEVICE_TIMEOUT 6  /* a kernel gave up on a bounded wait       */
+
+/* Number of configurations in the menu.
+ * Replaces: gemm_cfg_menu().size() (generated gemm_cfg_menu.h,
+ * src/gen_gemm_bank.py:239-251), seen through gemm_cfg_table_cpu
+ * (src/gemm_ext.cpp:108-120). */
+int gemm_num_cfgs(void);
+
+/* Number of knob columns per menu row (tile_m, tile_n, tile_k, stages,
+ * mma_sm, raster, group, split_k). Replaces the fixed 5 columns of
+ * gemm_cfg_table_cpu (src/gemm_ext.cpp:108-120). */
+int gemm_cfg_num_cols(void);
+
+/* Name of knob column `col` ("tile_m", ...), or NULL if out of range. */
+const char* gemm_cfg_col_name(int col);
+
+/* Copies menu row `cfg_id` into out[0..n). Returns GEMM_OK or
+ * GEMM_ERR_BAD_CFG / GEMM_ERR_INVALID_ARG.
+ * Replaces: one row of gemm_cfg_table_cpu (src/gemm_ext.cpp:108-120). */
+int gemm_cfg_row(int cfg_id, int* out, int n);
+
+/* Menu index of a knob tuple (n = gemm_cfg_num_cols()), or -1.
+ * Replaces: the exact-match 5-tuple compare of TRY_CFG
+ * (src/gemm_kernels.cuh:87-96) and the tuner's _TUPLE_TO_ID
+ * (infinite_dreams/tuner.py:25-27). */
+int gemm_cfg_find(const int* knobs, int n);
+
+/* Workspace bytes gemm_launch needs for this problem and config (0 when the
+ * config uses no split-K and both A and B are TMA-addressable: base 16-byte
+ * aligned and pitch a multiple of 8 elements).  The first
+ * gemm_workspace_counter_bytes() bytes of any non-empty workspace must be
+ * zero before its first use; every successful launch leaves them zero.
+ * No counterpart in the reference (it had no workspace, gemm_ext.cpp:35). */
+size_t gemm_workspace_bytes(const void* A, const void* B, int64_t M, int64_t N, int64_t K, int64_t lda,
+                            int64_t ldb, int cfg_id);
+
+/* Size of the zero-initialised ticket region at the head of a workspace. */
+size_t gemm_workspace_counter_bytes(void);
+
+/* Launch C = A*B with menu configuration cfg_id on `stream` (a cudaStream_t,
+ * NULL = legacy default stream).  Asynchronous.
+ * Replaces: gemm_forward_cfg (src/gemm_ext.cpp:95-106) ->
+ * gemm_forward_cuda_impl (src/gemm_ext.cpp:22-52) ->
+ * gemm_forward_cuda_launcher (src/gemm_cuda.cu:5-15). */
+int gemm_launch(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                int64_t ldb, int64_t ldc, int cfg_id, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Same as gemm_launch but the configuration is given as a knob tuple
+ * (n = gemm_cfg_num_cols()); a tuple that is not in the menu is an error.
+ * Replaces: gemm_forward(A,B,tile_m,tile_n,tile_k,tm,tn)
+ * (src/gemm_ext.cpp:57-93), which silently launched nothing on a miss. */
+int gemm_launch_knobs(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                      int64_t ldb, int64_t ldc, const int* knobs, int n, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/* A reasonable configuration for a shape when no tuned entry exists.
+ * No counterpart in the reference (its tuner had no per-shape dispatch). */
+int gemm_default_cfg(int64_t M, int64_t N, int64_t K);
+
+/* Reads and clears the device-side error word of `device` (synchronises
+ * that device).  *code receives the OR of the kernels' error bits (0 = none).
+ * Returns GEMM_OK, or GEMM_ERR_DEVICE_TIMEOUT when *code != 0.
+ * No counterpart in the reference (C10_CUDA_KERNEL_LAUNCH_CHECK only,
+ * src/gemm_ext.cpp:50). */
+int gemm_device_error(int device, int* code);
+
+/* Message for the calling thread's last failing call ("" if none). */
+const char* gemm_last_error(void);
+
+/* Human-readable name of a status code. */
+const char* gemm_status_string(int status);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* INFINITE_DREAMS_GEMM_SM100_H_ */

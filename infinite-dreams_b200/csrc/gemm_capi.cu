@@ -1,0 +1,459 @@
+// C ABI of the kernel bank (declared in include/gemm_sm100.h).
+//
+// Host side of the path the reference implements in src/gemm_ext.cpp:22-132
+// (validation, allocation, stream selection, config lookup) and
+// src/gemm_cuda.cu:5-15 (dispatch).  Differences, all deliberate:
+//  * the caller owns C and the workspace (no allocation in here);
+//  * a configuration is found by table lookup, and a miss is an error;
+//  * TMA descriptors are built per call from plain pointers and pitches;
+//  * operands whose base or pitch TMA cannot address are first repacked into
+//    the workspace by a copy kernel (pack_rows_f16).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/gemm_sm100.h"
+#include "gemm_bank_common.cuh"
+#include "generated/gemm_cfg_menu.inc"
+
+namespace idb {
+
+#define IDB_VARIANT(BN, ST)                                                                              \
+  cudaError_t launch_bn##BN##_s##ST(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c,   \
+                                    const GemmParams& p, int grid, cudaStream_t stream);
+#include "generated/gemm_variants.inc"
+#undef IDB_VARIANT
+
+struct Variant {
+  int bn;
+  int stages;
+  LaunchFn fn;
+};
+
+static const Variant kVariants[] = {
+#define IDB_VARIANT(BN, ST) {BN, ST, &launch_bn##BN##_s##ST},
+#include "generated/gemm_variants.inc"
+#undef IDB_VARIANT
+};
+
+// Copies a row-major fp16 matrix into a buffer whose row pitch is a multiple
+// of 8 elements (16 bytes) so that TMA can address it.  Used only when a
+// caller's A or B pitch / base address is not 16-byte aligned.
+__global__ void pack_rows_f16(const __half* __restrict__ src, long long lds, __half* __restrict__ dst,
+                              long long ldd, int rows, int cols) {
+  const long long chunks = (cols + 7) / 8;
+  const long long total = static_cast<long long>(rows) * chunks;
+  const unsigned short* s16 = reinterpret_cast<const unsigned short*>(src);
+  for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = idx / chunks;
+    const int c = static_cast<int>(idx - r * chunks) * 8;
+    const unsigned short* sp = s16 + r * lds + c;
+    unsigned short v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = (c + i < cols) ? sp[i] : static_cast<unsigned short>(0);
+    uint4 w;
+    w.x = v[0] | (static_cast<unsigned>(v[1]) << 16);
+    w.y = v[2] | (static_cast<unsigned>(v[3]) << 16);
+    w.z = v[4] | (static_cast<unsigned>(v[5]) << 16);
+    w.w = v[6] | (static_cast<unsigned>(v[7]) << 16);
+    *reinterpret_cast<uint4*>(dst + r * ldd + c) = w;
+  }
+}
+
+
+enum MenuCol { kColTileM = 0, kColTileN, kColTileK, kColStages, kColMmaSm, kColRaster, kColGroup, kColSplitK };
+
+__device__ int g_device_error = 0;
+
+namespace {
+
+thread_local std::string t_last_error;
+
+int fail(int status, const std::string& msg) {
+  t_last_error = msg;
+  return status;
+}
+
+int fail_cuda(cudaError_t e, const char* what) {
+  return fail(GEMM_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      return static_cast<EncodeTiledFn>(nullptr);
+    }
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+struct DeviceInfo {
+  int sms = 0;
+  int major = 0;
+  int minor = 0;
+  int max_smem_optin = 0;
+};
+
+constexpr int kMaxDevices = 64;
+DeviceInfo g_dev[kMaxDevices];
+std::once_flag g_dev_once[kMaxDevices];
+
+int device_info(DeviceInfo* out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(GEMM_ERR_UNSUPPORTED, "device index out of range");
+  std::call_once(g_dev_once[dev], [dev] {
+    DeviceInfo d;
+    cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev);
+    cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    g_dev[dev] = d;
+  });
+  *out = g_dev[dev];
+  if (out->major != 10 || out->minor != 0) {
+    return fail(GEMM_ERR_UNSUPPORTED, "the kernel bank is built for sm_100a (B200); device is sm_" +
+                                          std::to_string(out->major) + std::to_string(out->minor));
+  }
+  return GEMM_OK;
+}
+
+bool tma_addressable(const void* p, int64_t pitch_elems) {
+  return (reinterpret_cast<uintptr_t>(p) % 16u) == 0 && (pitch_elems % 8) == 0;
+}
+
+int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+
+struct Plan {
+  int tile_n = 0, stages = 0, raster = 0, group = 1, split_k = 1;
+  int tiles_m = 0, tiles_n = 0, num_tiles = 0, kb_total = 0;
+  bool pack_a = false, pack_b = false;
+  size_t off_partials = 0, off_pack_a = 0, off_pack_b = 0, total = 0;
+  int64_t lda_packed = 0, ldb_packed = 0;
+};
+
+constexpr size_t kCounterBytes = static_cast<size_t>(kCounterSlots) * sizeof(unsigned int);
+
+int make_plan(const void* A, const void* B, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+              int cfg_id, Plan* pl) {
+  if (cfg_id < 0 || cfg_id >= IDB_MENU_SIZE) {
+    return fail(GEMM_ERR_BAD_CFG, "cfg_id " + std::to_string(cfg_id) + " out of range [0, " +
+                                      std::to_string(IDB_MENU_SIZE) + ")");
+  }
+  if (M < 0 || N < 0 || K < 0) return fail(GEMM_ERR_INVALID_ARG, "M, N, K must be >= 0");
+  if (M > (1ll << 31) - 1 || N > (1ll << 31) - 1 || K > (1ll << 31) - 1) {
+    return fail(GEMM_ERR_UNSUPPORTED, "M, N, K must each be < 2^31");
+  }
+  const int* row = kMenu[cfg_id];
+  pl->tile_n = row[kColTileN];
+  pl->stages = row[kColStages];
+  pl->raster = row[kColRaster];
+  pl->group = row[kColGroup];
+  pl->tiles_m = static_cast<int>((M + kBM - 1) / kBM);
+  pl->tiles_n = static_cast<int>((N + pl->tile_n - 1) / pl->tile_n);
+  const int64_t tiles = static_cast<int64_t>(pl->tiles_m) * pl->tiles_n;
+  if (tiles > (1ll << 30)) return fail(GEMM_ERR_UNSUPPORTED, "too many output tiles");
+  pl->num_tiles = static_cast<int>(tiles);
+  pl->kb_total = static_cast<int>((K + kBK - 1) / kBK);
+  // A split count above the number of K blocks cannot give every slice work;
+  // it is clamped (the result is the same GEMM).
+  pl->split_k = row[kColSplitK];
+  if (pl->split_k > pl->kb_total) pl->split_k = pl->kb_total > 0 ? pl->kb_total : 1;
+  if (pl->split_k > 1 && pl->num_tiles > kCounterSlots) {
+    return fail(GEMM_ERR_UNSUPPORTED, "split-K supports at most 65536 output tiles");
+  }
+  pl->pack_a = M > 0 && K > 0 && !tma_addressable(A, lda);
+  pl->pack_b = N > 0 && K > 0 && !tma_addressable(B, ldb);
+  size_t off = 0;
+  if (pl->split_k > 1 || pl->pack_a || pl->pack_b) off = kCounterBytes;
+  if (pl->split_k > 1) {
+    pl->off_partials = off;
+    off += static_cast<size_t>(pl->num_tiles) * pl->split_k * kBM * pl->tile_n * sizeof(float);
+    off = static_cast<size_t>(round_up(static_cast<int64_t>(off), 256));
+  }
+  if (pl->pack_a) {
+    pl->lda_packed = round_up(K, 8);
+    pl->off_pack_a = off;
+    off += static_cast<size_t>(M) * pl->lda_packed * 2;
+    off = static_cast<size_t>(round_up(static_cast<int64_t>(off), 256));
+  }
+  if (pl->pack_b) {
+    pl->ldb_packed = round_up(N, 8);
+    pl->off_pack_b = off;
+    off += static_cast<size_t>(K) * pl->ldb_packed * 2;
+    off = static_cast<size_t>(round_up(static_cast<int64_t>(off), 256));
+  }
+  pl->total = off;
+  return GEMM_OK;
+}
+
+int encode_2d(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, int64_t pitch_elems, int box_inner,
+              int box_outer, const char* what) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(GEMM_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch_elems) * 2};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_outer)};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    return fail(GEMM_ERR_CUDA, std::string("cuTensorMapEncodeTiled(") + what + ") failed with CUresult " +
+                                   std::to_string(static_cast<int>(r)));
+  }
+  return GEMM_OK;
+}
+
+int launch_pack(const void* src, int64_t lds, void* dst, int64_t ldd, int64_t rows, int64_t cols,
+                cudaStream_t stream) {
+  const int64_t chunks = rows * ((cols + 7) / 8);
+  int64_t blocks = (chunks + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  if (blocks < 1) blocks = 1;
+  pack_rows_f16<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+      static_cast<const __half*>(src), lds, static_cast<__half*>(dst), ldd, static_cast<int>(rows),
+      static_cast<int>(cols));
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? GEMM_OK : fail_cuda(e, "pack_rows_f16 launch");
+}
+
+int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                int64_t ldc, int cfg_id, void* ws, size_t ws_bytes, void* stream_v) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  if (M < 0 || N < 0 || K < 0) return fail(GEMM_ERR_INVALID_ARG, "M, N, K must be >= 0");
+  if (M == 0 || N == 0) return GEMM_OK;
+  if (!A || !B || !C) return fail(GEMM_ERR_INVALID_ARG, "A, B and C must be non-null");
+  if (lda < K || ldb < N || ldc < N) {
+    return fail(GEMM_ERR_INVALID_ARG, "pitches must satisfy lda >= K, ldb >= N, ldc >= N");
+  }
+  if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) | reinterpret_cast<uintptr_t>(C)) % 2u) {
+    return fail(GEMM_ERR_INVALID_ARG, "A, B and C must be 2-byte aligned (fp16)");
+  }
+  Plan pl;
+  int st = make_plan(A, B, M, N, K, lda, ldb, cfg_id, &pl);
+  if (st != GEMM_OK) return st;
+  DeviceInfo dinfo;
+  st = device_info(&dinfo);
+  if (st != GEMM_OK) return st;
+  if (K == 0) {
+    // Empty reduction: C = 0 (the reference kernel's loop body never runs).
+    cudaError_t e = cudaMemset2DAsync(C, static_cast<size_t>(ldc) * 2, 0, static_cast<size_t>(N) * 2,
+                                      static_cast<size_t>(M), stream);
+    return e == cudaSuccess ? GEMM_OK : fail_cuda(e, "cudaMemset2DAsync");
+  }
+  if (pl.total > 0 && (ws == nullptr || ws_bytes < pl.total)) {
+    return fail(GEMM_ERR_WORKSPACE, "workspace of " + std::to_string(pl.total) + " bytes required, got " +
+                                        std::to_string(ws == nullptr ? 0 : ws_bytes));
+  }
+  if (pl.total > 0 && (reinterpret_cast<uintptr_t>(ws) % 256u) != 0) {
+    return fail(GEMM_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  }
+  const Variant* var = nullptr;
+  for (const Variant& v : kVariants) {
+    if (v.bn == pl.tile_n && v.stages == pl.stages) var = &v;
+  }
+  if (!var) return fail(GEMM_ERR_BAD_CFG, "no compiled kernel for this configuration");
+
+  uint8_t* wsb = static_cast<uint8_t*>(ws);
+  const void* a_src = A;
+  int64_t a_ld = lda;
+  const void* b_src = B;
+  int64_t b_ld = ldb;
+  if (pl.pack_a) {
+    st = launch_pack(A, lda, wsb + pl.off_pack_a, pl.lda_packed, M, K, stream);
+    if (st != GEMM_OK) return st;
+    a_src = wsb + pl.off_pack_a;
+    a_ld = pl.lda_packed;
+  }
+  if (pl.pack_b) {
+    st = launch_pack(B, ldb, wsb + pl.off_pack_b, pl.ldb_packed, K, N, stream);
+    if (st != GEMM_OK) return st;
+    b_src = wsb + pl.off_pack_b;
+    b_ld = pl.ldb_packed;
+  }
+
+  CUtensorMap tmA, tmB, tmC;
+  std::memset(&tmC, 0, sizeof(tmC));
+  st = encode_2d(&tmA, a_src, K, M, a_ld, kBK, kBM, "A");
+  if (st != GEMM_OK) return st;
+  st = encode_2d(&tmB, b_src, N, K, b_ld, 64, kBK, "B");
+  if (st != GEMM_OK) return st;
+  const bool c_tma = tma_addressable(C, ldc);
+  if (c_tma) {
+    st = encode_2d(&tmC, C, N, M, ldc, kStoreCols, kStoreRows, "C");
+    if (st != GEMM_OK) return st;
+  }
+
+  int* err_word = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&err_word), g_device_error);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaGetSymbolAddress(g_device_error)");
+
+  GemmParams p;
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.tiles_m = pl.tiles_m;
+  p.tiles_n = pl.tiles_n;
+  p.num_tiles = pl.num_tiles;
+  p.split_k = pl.split_k;
+  p.kb_total = pl.kb_total;
+  p.raster = pl.raster;
+  p.group = pl.group;
+  p.c_tma = c_tma ? 1 : 0;
+  p.C = static_cast<__half*>(C);
+  p.ldc = ldc;
+  p.partials = pl.split_k > 1 ? reinterpret_cast<float*>(wsb + pl.off_partials) : nullptr;
+  p.counters = pl.split_k > 1 ? reinterpret_cast<unsigned int*>(wsb) : nullptr;
+  p.err = err_word;
+
+  const int64_t units = static_cast<int64_t>(pl.num_tiles) * pl.split_k;
+  const int grid = static_cast<int>(units < dinfo.sms ? units : dinfo.sms);
+  e = var->fn(tmA, tmB, tmC, p, grid, stream);
+  if (e != cudaSuccess) return fail_cuda(e, "gemm kernel launch");
+  return GEMM_OK;
+}
+
+}  // namespace
+}  // namespace idb
+
+using namespace idb;
+
+extern "C" {
+
+int gemm_num_cfgs(void) { return IDB_MENU_SIZE; }
+
+int gemm_cfg_num_cols(void) { return IDB_MENU_COLS; }
+
+const char* gemm_cfg_col_name(int col) {
+  if (col < 0 || col >= IDB_MENU_COLS) return nullptr;
+  return kMenuColumns[col];
+}
+
+int gemm_cfg_row(int cfg_id, int* out, int n) {
+  if (cfg_id < 0 || cfg_id >= IDB_MENU_SIZE) return fail(GEMM_ERR_BAD_CFG, "cfg_id out of range");
+  if (!out || n < 0) return fail(GEMM_ERR_INVALID_ARG, "out must be non-null and n >= 0");
+  for (int i = 0; i < n && i < IDB_MENU_COLS; ++i) out[i] = kMenu[cfg_id][i];
+  return GEMM_OK;
+}
+
+int gemm_cfg_find(const int* knobs, int n) {
+  if (!knobs || n != IDB_MENU_COLS) return -1;
+  // The menu is sorted lexicographically: binary search.
+  int lo = 0, hi = IDB_MENU_SIZE - 1;
+  while (lo <= hi) {
+    const int mid = (lo + hi) / 2;
+    int cmp = 0;
+    for (int i = 0; i < IDB_MENU_COLS && cmp == 0; ++i) {
+      cmp = (kMenu[mid][i] < knobs[i]) ? -1 : (kMenu[mid][i] > knobs[i]) ? 1 : 0;
+    }
+    if (cmp == 0) return mid;
+    if (cmp < 0) lo = mid + 1;
+    else hi = mid - 1;
+  }
+  return -1;
+}
+
+size_t gemm_workspace_bytes(const void* A, const void* B, int64_t M, int64_t N, int64_t K, int64_t lda,
+                            int64_t ldb, int cfg_id) {
+  Plan pl;
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  if (make_plan(A, B, M, N, K, lda, ldb, cfg_id, &pl) != GEMM_OK) return 0;
+  return pl.total;
+}
+
+size_t gemm_workspace_counter_bytes(void) { return kCounterBytes; }
+
+int gemm_launch(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                int64_t ldc, int cfg_id, void* workspace, size_t workspace_bytes, void* stream) {
+  t_last_error.clear();
+  return launch_impl(A, B, C, M, N, K, lda, ldb, ldc, cfg_id, workspace, workspace_bytes, stream);
+}
+
+int gemm_launch_knobs(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                      int64_t ldb, int64_t ldc, const int* knobs, int n, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  t_last_error.clear();
+  const int id = gemm_cfg_find(knobs, n);
+  if (id < 0) {
+    std::string t = "(";
+    for (int i = 0; knobs && i < n; ++i) t += (i ? "," : "") + std::to_string(knobs[i]);
+    return fail(GEMM_ERR_BAD_CFG, "knob tuple " + t + ") is not in the kernel bank menu");
+  }
+  return launch_impl(A, B, C, M, N, K, lda, ldb, ldc, id, workspace, workspace_bytes, stream);
+}
+
+int gemm_default_cfg(int64_t M, int64_t N, int64_t K) {
+  // Heuristic: the widest tile whose wave count is reasonable; split K when
+  // the output has too few tiles to occupy the 148 SMs.
+  const int kSms = 148;
+  int tile_n = 256, stages = 4;
+  const int64_t tm = (M + kBM - 1) / kBM;
+  if (tm * ((N + 255) / 256) < kSms) {
+    tile_n = 128;
+    stages = 6;
+  }
+  const int64_t tiles = tm * ((N + tile_n - 1) / tile_n);
+  const int64_t kb = (K + kBK - 1) / kBK;
+  int split = 1;
+  if (tiles < kSms / 2 && kb >= 8) {
+    const int choices[] = {16, 12, 8, 6, 4, 3, 2};
+    for (int c : choices) {
+      if (tiles * c <= kSms + kSms / 4 && kb / c >= 4) {
+        split = c;
+        break;
+      }
+    }
+  }
+  int knobs[IDB_MENU_COLS] = {kBM, tile_n, kBK, stages, 1, 0, 8, split};
+  return gemm_cfg_find(knobs, IDB_MENU_COLS);
+}
+
+int gemm_device_error(int device, int* code) {
+  t_last_error.clear();
+  int prev = 0;
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaGetDevice");
+  if (device != prev && (e = cudaSetDevice(device)) != cudaSuccess) return fail_cuda(e, "cudaSetDevice");
+  int v = 0;
+  const int zero = 0;
+  e = cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int));
+  if (e == cudaSuccess && v != 0) e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+  if (device != prev) cudaSetDevice(prev);
+  if (e != cudaSuccess) return fail_cuda(e, "reading the device error word");
+  if (code) *code = v;
+  if (v != 0) return fail(GEMM_ERR_DEVICE_TIMEOUT, "a kernel gave up on a bounded wait (error bits " +
+                                                       std::to_string(v) + ")");
+  return GEMM_OK;
+}
+
+const char* gemm_last_error(void) { return t_last_error.c_str(); }
+
+const char* gemm_status_string(int status) {
+  switch (status) {
+    case GEMM_OK: return "GEMM_OK";
+    case GEMM_ERR_INVALID_ARG: return "GEMM_ERR_INVALID_ARG";
+    case GEMM_ERR_BAD_CFG: return "GEMM_ERR_BAD_CFG";
+    case GEMM_ERR_WORKSPACE: return "GEMM_ERR_WORKSPACE";
+    case GEMM_ERR_CUDA: return "GEMM_ERR_CUDA";
+    case GEMM_ERR_UNSUPPORTED: return "GEMM_ERR_UNSUPPORTED";
+    case GEMM_ERR_DEVICE_TIMEOUT: return "GEMM_ERR_DEVICE_TIMEOUT";
+    default: return "GEMM_ERR_UNKNOWN";
+  }
+}
+
+}  // extern "C"

@@ -1,0 +1,440 @@
+// FP16-in / FP32-accumulate / FP16-out GEMM  C[M,N] = A[M,K] * B[K,N]  for sm_100a.
+//
+// Replaces the reference's SIMT kernel `gemm_tiled_reg<TILE_M,TILE_N,TILE_K,TM,TN>`
+// (src/gemm_kernels.cuh:6-83): same operand layout (all row-major, fp16 in,
+// fp32 accumulate, fp16 out rounded to nearest as __float2half does, zero
+// contribution from rows/columns outside M/N/K), built the Blackwell way:
+//
+//   warp 0      TMA producer: A box [128 x 64] (K-major, 128B swizzle) and
+//               B boxes [64 x 64] (N-major, 128B swizzle) per pipeline stage,
+//               completing on a `full` mbarrier.
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
+//               (M=128, N=BN, K=16 per instruction), frees smem stages with
+//               tcgen05.commit -> `empty` mbarrier, hands finished accumulators
+//               to the epilogue with tcgen05.commit -> `tmem_full`.
+//   warps 2..5  epilogue: tcgen05.ld (32 lanes x 32 columns per warp), fp16
+//               conversion, 128B-swizzled smem staging, TMA store (or a
+//               coalesced st.global path when C's row pitch is not 16-byte
+//               aligned).  Split-K partials go to an fp32 workspace; the last
+//               CTA of a tile (atomic ticket, no spinning) sums the partials
+//               in split order and writes C.
+//
+// The kernel is persistent (grid <= #SMs, static round-robin over work units)
+// and double-buffers the TMEM accumulator (2 x BN columns), so the epilogue of
+// one tile overlaps the mainloop of the next.  Every mbarrier wait is bounded
+// (see sm100_ptx.cuh); a timeout raises a CTA abort flag and an error bit in
+// the library's device error word, and every role drains what it started
+// before the CTA frees TMEM and exits.
+#pragma once
+#include "sm100_ptx.cuh"
+
+namespace idb {
+
+constexpr int kBM = 128;          // rows per CTA tile: one M=128 tcgen05.mma
+constexpr int kBK = 64;           // K per pipeline stage: one 128-byte fp16 swizzle row
+constexpr int kUmmaK = 16;        // K per tcgen05.mma.kind::f16
+constexpr int kEpiWarps = 4;      // one warpgroup covers the 128 TMEM lanes
+constexpr int kNumThreads = 64 + 32 * kEpiWarps;
+constexpr int kStoreRows = 32;    // rows per epilogue store box (one warp's TMEM lanes)
+constexpr int kStoreCols = 64;    // columns per epilogue store box (128 bytes)
+constexpr int kCounterSlots = 65536;  // split-K tile tickets at the head of the workspace
+
+struct GemmParams {
+  int M, N, K;
+  int tiles_m, tiles_n;
+  int num_tiles;
+  int split_k;    // >= 1, <= kb_total
+  int kb_total;   // ceil(K / kBK)
+  int raster;     // 0: groups of `group` tile-rows, M fastest; 1: groups of tile-columns, N fastest
+  int group;      // >= 1
+  int c_tma;      // 1: TMA-store epilogue; 0: coalesced st.global epilogue (any pitch)
+  __half* C;
+  long long ldc;
+  float* partials;          // split-K fp32 partial tiles (tile, split, 128 x BN)
+  unsigned int* counters;   // split-K tickets, zero on entry and on exit
+  int* err;                 // device error word
+};
+
+template <int BN, int STAGES>
+struct SmemPlan {
+  static constexpr int kABytes = kBM * kBK * 2;                 // 16 KiB
+  static constexpr int kBBytes = kBK * BN * 2;                  // BN x 128 B
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kCBufBytes = kStoreRows * kStoreCols * 2;  // 4 KiB
+  static constexpr int kCBytes = kEpiWarps * 2 * kCBufBytes;      // double-buffered per warp
+  static constexpr int kOffA = 0;
+  static constexpr int kOffB = kOffA + STAGES * kABytes;
+  static constexpr int kOffC = kOffB + STAGES * kBBytes;
+  static constexpr int kOffBar = kOffC + kCBytes;
+  static constexpr int kNumBars = 2 * STAGES + 4 + 1;           // full, empty, tmem_full[2], tmem_empty[2], done
+  static constexpr int kOffMisc = kOffBar + kNumBars * 8;
+  static constexpr int kUsed = kOffMisc + 16;
+  static constexpr int kDynamicBytes = kUsed + 1024;            // slack for 1024-byte alignment
+  static constexpr uint32_t kTmemCols = (2 * BN <= 32)    ? 32
+                                        : (2 * BN <= 64)  ? 64
+                                        : (2 * BN <= 128) ? 128
+                                        : (2 * BN <= 256) ? 256
+                                                          : 512;
+  static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be 64..256 in steps of 64");
+  static_assert(kOffB % 1024 == 0 && kOffC % 1024 == 0, "swizzled buffers need 1024-byte alignment");
+};
+
+// Work unit -> (tile row, tile column, split index).
+__device__ __forceinline__ void decode_unit(const GemmParams& p, int u, int& tm, int& tn, int& ks) {
+  ks = u % p.split_k;
+  const int t = u / p.split_k;
+  if (p.raster == 0) {
+    const int per_group = p.group * p.tiles_n;
+    const int g = t / per_group;
+    const int first = g * p.group;
+    const int gs = min(p.tiles_m - first, p.group);
+    const int r = t - g * per_group;
+    tm = first + r % gs;
+    tn = r / gs;
+  } else {
+    const int per_group = p.group * p.tiles_m;
+    const int g = t / per_group;
+    const int first = g * p.group;
+    const int gs = min(p.tiles_n - first, p.group);
+    const int r = t - g * per_group;
+    tn = first + r % gs;
+    tm = r / gs;
+  }
+}
+
+__device__ __forceinline__ void split_range(const GemmParams& p, int ks, int& kb0, int& kb1) {
+  kb0 = static_cast<int>((static_cast<long long>(ks) * p.kb_total) / p.split_k);
+  kb1 = static_cast<int>((static_cast<long long>(ks + 1) * p.kb_total) / p.split_k);
+}
+
+// Converts 64 fp32 values of one row to fp16 and writes them as row `lane`
+// of a [32 x 64] fp16 staging box in the TMA 128-byte swizzle layout.
+__device__ __forceinline__ void stage_row_sw128(uint8_t* buf, int lane, const float (&f)[64]) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint4 w;
+    w.x = pack_half2(f[8 * c + 0], f[8 * c + 1]);
+    w.y = pack_half2(f[8 * c + 2], f[8 * c + 3]);
+    w.z = pack_half2(f[8 * c + 4], f[8 * c + 5]);
+    w.w = pack_half2(f[8 * c + 6], f[8 * c + 7]);
+    const int phys = c ^ (lane & 7);
+    *reinterpret_cast<uint4*>(buf + lane * 128 + phys * 16) = w;
+  }
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kNumThreads, 1)
+    gemm_f16_sm100(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
+  using Plan = SmemPlan<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem + Plan::kOffA;
+  uint8_t* sB = smem + Plan::kOffB;
+  uint8_t* sC = smem + Plan::kOffC;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + Plan::kOffBar);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint64_t* done_bar = tempty_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Plan::kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
+
+  const int warp = static_cast<int>(threadIdx.x >> 5);
+  const int lane = static_cast<int>(threadIdx.x & 31);
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(&tfull_bar[0], 1);
+    mbar_init(&tfull_bar[1], 1);
+    mbar_init(&tempty_bar[0], kEpiWarps);
+    mbar_init(&tempty_bar[1], kEpiWarps);
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    *last_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+    if (p.c_tma) prefetch_tmap(&tmC);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Plan::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_units = p.num_tiles * p.split_k;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        int tm, tn, ks, kb0, kb1;
+        decode_unit(p, u, tm, tn, ks);
+        split_range(p, ks, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full_bar[stage], Plan::kStageBytes);
+          tma_load_2d(sA + stage * Plan::kABytes, &tmA, &full_bar[stage], kb * kBK, tm * kBM);
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j) {
+            tma_load_2d(sB + stage * Plan::kBBytes + j * (kBK * 128), &tmB, &full_bar[stage], tn * BN + j * 64,
+                        kb * kBK);
+          }
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicOr(p.err, kDevErrTimeoutProducer);
+      }
+      // Drain: the last min(issued, STAGES) fills must have landed before the
+      // CTA may exit (an in-flight TMA write into a retired CTA is undefined).
+      const int outstanding = issued < STAGES ? issued : STAGES;
+      for (int i = 0; i < outstanding; ++i) {
+        stage = (stage == 0) ? STAGES - 1 : stage - 1;
+        if (stage == STAGES - 1) phase ^= 1u;
+        uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&full_bar[stage], phase)) {
+          if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            atomicOr(p.err, kDevErrTimeoutTeardown);
+            break;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(kBM, BN, /*a_mn_major=*/false, /*b_mn_major=*/true);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        int tm, tn, ks, kb0, kb1;
+        decode_unit(p, u, tm, tn, ks);
+        split_range(p, ks, kb0, kb1);
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * Plan::kABytes);
+          const uint32_t b0 = smem_u32(sB + stage * Plan::kBBytes);
+#pragma unroll
+          for (int j = 0; j < kBK / kUmmaK; ++j) {
+            // A: K-major, advance 16 elements (32 B) inside the swizzled row.
+            const uint64_t ad = smem_desc_sw128(a0 + j * (kUmmaK * 2), 16, 1024);
+            // B: N-major, advance 16 K-rows (2 KiB); atoms of 64 columns are kBK*128 B apart.
+            const uint64_t bd = smem_desc_sw128(b0 + j * (kUmmaK * 128), kBK * 128, 1024);
+            mma_f16_ss(d_tmem, ad, bd, idesc, (kb > kb0 || j > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty_bar[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&tfull_bar[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicOr(p.err, kDevErrTimeoutMma);
+      }
+      // Every MMA this thread issued must retire before TMEM is freed.
+      mma_commit(done_bar);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(done_bar, 0)) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          atomicOr(p.err, kDevErrTimeoutTeardown);
+          break;
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp & 3;               // TMEM lane quarter this warp may access
+    const int row = ew * 32 + lane;        // row inside the 128-row tile
+    const bool leader = (threadIdx.x == 64);
+    uint8_t* cbufs = sC + ew * 2 * Plan::kCBufBytes;
+    int cb = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
+      int tm, tn, ks;
+      decode_unit(p, u, tm, tn, ks);
+      // All four warps take the same decision, so none is left waiting at a
+      // later named barrier if another gave up.
+      ok = named_bar_and(1, 32 * kEpiWarps, mbar_wait(&tfull_bar[acc], acc_phase, abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      const int grow = tm * kBM + row;
+      const bool row_ok = grow < p.M;
+      const int tile = u / p.split_k;
+      bool write_c = true;
+      float* slots = nullptr;
+      if (p.split_k > 1) {
+        slots = p.partials + static_cast<size_t>(tile) * p.split_k * (kBM * BN);
+        float4* mine = reinterpret_cast<float4*>(slots + static_cast<size_t>(ks) * (kBM * BN));
+#pragma unroll 1
+        for (int c32 = 0; c32 < BN / 32; ++c32) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tbase + c32 * 32, v);
+          tmem_ld_wait();
+          if (row_ok) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              mine[(c32 * 8 + q) * kBM + row] =
+                  make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                              __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]));
+            }
+          }
+        }
+        __threadfence();
+        named_bar_sync(1, 32 * kEpiWarps);
+        if (leader) {
+          const unsigned old = atomicAdd(&p.counters[tile], 1u);
+          *last_flag = (old == static_cast<unsigned>(p.split_k - 1)) ? 1 : 0;
+        }
+        named_bar_sync(1, 32 * kEpiWarps);
+        write_c = (*last_flag != 0);
+        if (write_c) __threadfence();
+      }
+      if (write_c) {
+#pragma unroll 1
+        for (int c64 = 0; c64 < BN / 64; ++c64) {
+          float f[64];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(tbase + c64 * 64 + h * 32, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) f[h * 32 + i] = __uint_as_float(v[i]);
+          }
+          if (p.split_k > 1) {
+            // Sum the partials in split order (deterministic whichever CTA is last).
+            float s[64];
+#pragma unroll
+            for (int i = 0; i < 64; ++i) s[i] = 0.0f;
+            for (int s2 = 0; s2 < p.split_k; ++s2) {
+              if (s2 == ks) {
+#pragma unroll
+                for (int i = 0; i < 64; ++i) s[i] += f[i];
+              } else if (row_ok) {
+                const float4* src = reinterpret_cast<const float4*>(slots + static_cast<size_t>(s2) * (kBM * BN));
+#pragma unroll
+                for (int q = 0; q < 16; ++q) {
+                  const float4 x = __ldcg(&src[(c64 * 16 + q) * kBM + row]);
+                  s[4 * q] += x.x;
+                  s[4 * q + 1] += x.y;
+                  s[4 * q + 2] += x.z;
+                  s[4 * q + 3] += x.w;
+                }
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < 64; ++i) f[i] = s[i];
+          }
+          uint8_t* buf = cbufs + cb * Plan::kCBufBytes;
+          if (p.c_tma) {
+            if (lane == 0) bulk_wait_group_read<1>();
+            __syncwarp();
+          }
+          stage_row_sw128(buf, lane, f);
+          const int col0 = tn * BN + c64 * 64;
+          if (p.c_tma) {
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              // A box that starts past the edge has nothing to write; skip it
+              // but still close a (possibly empty) bulk group so that the
+              // wait_group.read<1> accounting above stays per buffer.
+              const int row0 = tm * kBM + ew * 32;
+              if (row0 < p.M && col0 < p.N) tma_store_2d(&tmC, buf, col0, row0);
+              bulk_commit_group();
+            }
+          } else {
+            __syncwarp();
+            const int row0 = tm * kBM + ew * 32;
+            for (int r = 0; r < kStoreRows; ++r) {
+              const int gr = row0 + r;
+              if (gr >= p.M) break;
+              __half* crow = p.C + static_cast<long long>(gr) * p.ldc;
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int col = h * 32 + lane;
+                const int gc = col0 + col;
+                if (gc < p.N) {
+                  const uint8_t* src = buf + r * 128 + (((col >> 3) ^ (r & 7)) << 4) + (col & 7) * 2;
+                  crow[gc] = *reinterpret_cast<const __half*>(src);
+                }
+              }
+            }
+            __syncwarp();
+          }
+          cb ^= 1;
+        }
+        if (p.split_k > 1 && leader) p.counters[tile] = 0u;  // leave the ticket zero for the next launch
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    if (!ok) {
+      *abort_flag = 1;
+      atomicOr(p.err, kDevErrTimeoutEpilogue);
+    }
+    if (p.c_tma && lane == 0) bulk_wait_group<0>();
+  }
+
+  // ------------------------------------------------------------ teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Plan::kTmemCols);
+  }
+}
+
+}  // namespace idb

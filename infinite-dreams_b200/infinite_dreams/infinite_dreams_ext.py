@@ -1,0 +1,154 @@
+"""Drop-in for the reference's compiled extension ``infinite_dreams_ext``.
+
+The reference module (src/gemm_ext.cpp:123-132) exports three functions; the
+same three names are exported here with the same argument meaning and the
+same error behaviour (``RuntimeError`` with the reference's messages), backed
+by the sm_100a kernel bank through its C ABI (include/gemm_sm100.h):
+
+* ``gemm_forward(A, B, tile_m, tile_n, tile_k, stages, mma_sm=1, raster=0,
+  group=8, split_k=1)`` -- explicit knobs (src/gemm_ext.cpp:57-93).  The
+  reference's knobs were (tile_m, tile_n, tile_k, tm, tn); the register
+  micro-tile (tm, tn) has no meaning for tcgen05, so the positions after
+  tile_k carry the Blackwell knobs.  A tuple that is not in the menu raises
+  (the reference returned an uninitialised tensor, gemm_ext.cpp:35 + F7).
+* ``gemm_forward_cfg(A, B, cfg_id)`` -- menu id (src/gemm_ext.cpp:95-106).
+* ``gemm_cfg_table_cpu()`` -- the menu as a CPU int32 tensor
+  ``[num_cfg, len(CFG_COLUMNS)]`` (src/gemm_ext.cpp:108-120).
+
+Like the reference, inputs are made contiguous, C is allocated from torch's
+caching allocator on A's device, and the launch is asynchronous on the
+current stream.  Split-K / repacking workspace is cached per (device, stream)
+and zero-initialised once, as the C ABI requires.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from typing import Dict, Optional, Tuple
+
+import torch
+
+from . import _capi
+from ._capi import GemmError, lib
+
+CFG_COLUMNS: Tuple[str, ...] = tuple(_capi.menu()[0])
+NUM_CFG: int = int(lib.gemm_num_cfgs())
+
+_ws_lock = threading.Lock()
+_workspaces: Dict[Tuple[int, int], torch.Tensor] = {}
+
+
+def _workspace(device: torch.device, stream: torch.cuda.Stream, nbytes: int) -> Tuple[int, int]:
+    if nbytes == 0:
+        return 0, 0
+    key = (device.index, stream.cuda_stream)
+    with _ws_lock:
+        ws = _workspaces.get(key)
+        if ws is None or ws.numel() < nbytes:
+            # Grow geometrically; zeros satisfies the "ticket region is zero" contract.
+            size = max(nbytes, 0 if ws is None else 2 * ws.numel())
+            with torch.cuda.stream(stream):
+                ws = torch.zeros(size, dtype=torch.uint8, device=device)
+            _workspaces[key] = ws
+    return ws.data_ptr(), ws.numel()
+
+
+def reset_workspaces() -> None:
+    """Drops cached workspaces (needed after a device-side timeout)."""
+    with _ws_lock:
+        _workspaces.clear()
+
+
+def _check_inputs(A: torch.Tensor, B: torch.Tensor) -> None:
+    # Same checks and messages as src/gemm_ext.cpp:66-73,86.
+    if not isinstance(A, torch.Tensor) or not A.is_cuda:
+        raise RuntimeError("A must be CUDA tensor")
+    if not isinstance(B, torch.Tensor) or not B.is_cuda:
+        raise RuntimeError("B must be CUDA tensor")
+    if A.dtype != torch.float16:
+        raise RuntimeError("A must be float16")
+    if B.dtype != torch.float16:
+        raise RuntimeError("B must be float16")
+    if A.dim() != 2:
+        raise RuntimeError("A must be 2D (M x K)")
+    if B.dim() != 2:
+        raise RuntimeError("B must be 2D (K x N)")
+    if A.size(1) != B.size(0):
+        raise RuntimeError("Inner dimensions must match: A is (M x K), B is (K x N)")
+    if A.get_device() != B.get_device():
+        raise RuntimeError("A and B must be on the same CUDA device")
+
+
+def _launch(A: torch.Tensor, B: torch.Tensor, cfg_id: int, out: Optional[torch.Tensor]) -> torch.Tensor:
+    M, K = int(A.size(0)), int(A.size(1))
+    N = int(B.size(1))
+    dev = A.device
+    with torch.cuda.device(dev):
+        A = A.contiguous()
+        B = B.contiguous()
+        if out is None:
+            C = torch.empty((M, N), dtype=torch.float16, device=dev)
+        else:
+            if (out.dtype != torch.float16 or tuple(out.shape) != (M, N) or out.device != dev
+                    or not out.is_contiguous()):
+                raise RuntimeError("out must be a contiguous float16 (M x N) tensor on A's device")
+            C = out
+        stream = torch.cuda.current_stream(dev)
+        need = int(lib.gemm_workspace_bytes(A.data_ptr(), B.data_ptr(), M, N, K, K, N, cfg_id))
+        ws_ptr, ws_len = _workspace(dev, stream, need)
+        st = lib.gemm_launch(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, K, N, N, cfg_id,
+                             ws_ptr or None, ws_len, stream.cuda_stream or None)
+        _capi.check(st, "gemm_launch")
+    return C
+
+
+def gemm_forward(A: torch.Tensor, B: torch.Tensor, tile_m: int, tile_n: int, tile_k: int, stages: int,
+                 mma_sm: int = 1, raster: int = 0, group: int = 8, split_k: int = 1,
+                 *, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """FP16 GEMM forward (CUDA) with explicit knobs; the tuple must be in the menu."""
+    _check_inputs(A, B)
+    if tile_m <= 0 or tile_n <= 0 or tile_k <= 0:
+        raise RuntimeError("tile_m/tile_n/tile_k must be > 0")
+    if stages <= 0 or mma_sm <= 0 or group <= 0 or split_k <= 0:
+        raise RuntimeError("stages/mma_sm/group/split_k must be > 0")
+    knobs = (tile_m, tile_n, tile_k, stages, mma_sm, raster, group, split_k)
+    cfg_id = _capi.cfg_find(knobs)
+    if cfg_id < 0:
+        raise RuntimeError(f"knob tuple {knobs} is not in the kernel bank menu "
+                           f"(columns {', '.join(CFG_COLUMNS)})")
+    return _launch(A, B, cfg_id, out)
+
+
+def gemm_forward_cfg(A: torch.Tensor, B: torch.Tensor, cfg_id: int, *,
+                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """FP16 GEMM forward (CUDA) using cfg_id from the static menu."""
+    if cfg_id < 0:
+        raise RuntimeError("cfg_id must be >= 0")
+    if cfg_id >= NUM_CFG:
+        raise RuntimeError("cfg_id out of range")
+    _check_inputs(A, B)
+    return _launch(A, B, int(cfg_id), out)
+
+
+def gemm_cfg_table_cpu() -> torch.Tensor:
+    """CPU int32 tensor [num_cfg, len(CFG_COLUMNS)], columns CFG_COLUMNS."""
+    cols, rows = _capi.menu()
+    return torch.tensor(rows, dtype=torch.int32).reshape(len(rows), len(cols))
+
+
+def default_cfg(M: int, N: int, K: int) -> int:
+    return int(lib.gemm_default_cfg(M, N, K))
+
+
+def check_device_errors(device: Optional[int] = None) -> None:
+    """Raises if a kernel on `device` gave up on a bounded wait (synchronises)."""
+    dev = torch.cuda.current_device() if device is None else int(device)
+    code = ctypes.c_int(0)
+    st = lib.gemm_device_error(dev, ctypes.byref(code))
+    if st != _capi.GEMM_OK:
+        reset_workspaces()
+        raise GemmError(st, f"device {dev}: kernel error bits {code.value}")
+
+
+__all__ = ["gemm_forward", "gemm_forward_cfg", "gemm_cfg_table_cpu", "CFG_COLUMNS", "NUM_CFG",
+           "default_cfg", "check_device_errors", "GemmError", "reset_workspaces"]

@@ -1,0 +1,186 @@
+/*
+ * ORACLE -- test infrastructure only.  Not part of the product; nothing in
+ * the shipped library links or calls it.  Only tests/, the smoke check and
+ * the CPU-baseline leg of bench.py use it, and only as the checker.
+ *
+ * CPU restatement of the arithmetic of the reference kernel
+ * gemm_tiled_reg<TILE_M,TILE_N,TILE_K,TM,TN> (src/gemm_kernels.cuh:6-83):
+ *
+ *   * every output element C[r][c] owns one fp32 accumulator initialised to
+ *     0 (`float acc[TM][TN] = {0}`, :16);
+ *   * the accumulator is updated once per k, in increasing k order: the
+ *     outer `for k0` loop (:18) walks K tiles in order and the inner
+ *     `for kk` loop (:41) walks the tile in order, so k = k0 + kk ascends;
+ *   * each update is acc += float(A[r][k]) * float(B[k][c]) (:48, :54, :61).
+ *     An fp16 x fp16 product is exact in fp32 (11 + 11 significand bits), so
+ *     whether nvcc contracts the update into an FFMA does not change the
+ *     result: both round the exact sum once;
+ *   * positions with r >= M or k >= K or c >= N read 0 (:27, :35), which adds
+ *     exact zeros and does not change the sum;
+ *   * the result is converted with __float2half (:79), round to nearest even.
+ *   --use_fast_math (setup.py:14) flushes fp32 subnormals, but every nonzero
+ *     partial sum of fp16 products is a multiple of 2^-48, far above the fp32
+ *     subnormal range, so flushing never triggers.
+ *
+ * Hence the result is independent of the reference's tile configuration and
+ * this loop reproduces it bit for bit (pinned against the reference kernel
+ * compiled from source, see oracle/ref_bank.cu and tests/golden/).
+ */
+#include <math.h>
+#include <pthread.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* fp16 bits -> fp32, exact. */
+float oracle_f16_to_f32(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  const uint32_t e = (h >> 10) & 0x1Fu;
+  const uint32_t m = h & 0x3FFu;
+  uint32_t bits;
+  if (e == 0) {
+    /* zero or subnormal: m * 2^-24, exact in fp32 */
+    float v = (float)m * 5.9604644775390625e-08f;
+    return sign ? -v : v;
+  } else if (e == 31) {
+    bits = sign | 0x7F800000u | (m << 13);
+  } else {
+    bits = sign | ((e + 112u) << 23) | (m << 13);
+  }
+  float f;
+  memcpy(&f, &bits, 4);
+  return f;
+}
+
+/* fp32 -> fp16 bits, IEEE round to nearest, ties to even. */
+uint16_t oracle_f32_to_f16(float f) {
+  uint32_t x;
+  memcpy(&x, &f, 4);
+  const uint16_t sign = (uint16_t)((x >> 16) & 0x8000u);
+  const uint32_t ax = x & 0x7FFFFFFFu;
+  if (ax > 0x7F800000u) return 0x7FFFu;          /* NaN (canonical) */
+  if (ax >= 0x477FF000u) return sign | 0x7C00u;  /* >= 65520 rounds to infinity */
+  if (ax < 0x38800000u) {
+    /* below 2^-14: half subnormal (or zero / smallest normal after rounding).
+     * |f| * 2^24 is exact; rint rounds half to even in the default mode. */
+    float a;
+    memcpy(&a, &ax, 4);
+    const float q = rintf(a * 16777216.0f);
+    return sign | (uint16_t)q;
+  }
+  /* normal: rebias the exponent (127 -> 15) and drop 13 mantissa bits with RNE */
+  const uint32_t u = ax - (112u << 23);
+  uint32_t h = u >> 13;
+  const uint32_t rem = u & 0x1FFFu;
+  if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) h += 1u;
+  return sign | (uint16_t)h;
+}
+
+/* One worker's share: rows [r0, r1) x columns [c0, c1). */
+typedef struct {
+  const uint16_t* A;
+  const uint16_t* B;
+  uint16_t* C;
+  int64_t M, N, K, lda, ldb, ldc;
+  int64_t r0, r1, c0, c1;
+} oracle_job;
+
+#define ORACLE_KBLK 64
+
+static void* oracle_worker(void* arg) {
+  const oracle_job* j = (const oracle_job*)arg;
+  const int64_t w = j->c1 - j->c0;
+  const int64_t nr = j->r1 - j->r0;
+  if (w <= 0 || nr <= 0) return NULL;
+  float* acc = (float*)calloc((size_t)(nr * w), sizeof(float));
+  float* bf = (float*)malloc((size_t)(ORACLE_KBLK * w) * sizeof(float));
+  if (!acc || !bf) {
+    free(acc);
+    free(bf);
+    return (void*)1;
+  }
+  for (int64_t k0 = 0; k0 < j->K; k0 += ORACLE_KBLK) {
+    const int64_t kn = (j->K - k0) < ORACLE_KBLK ? (j->K - k0) : ORACLE_KBLK;
+    /* convert this K block of B (our column slice) to fp32 once */
+    for (int64_t kk = 0; kk < kn; ++kk) {
+      const uint16_t* brow = j->B + (k0 + kk) * j->ldb + j->c0;
+      float* dst = bf + kk * w;
+      for (int64_t c = 0; c < w; ++c) dst[c] = oracle_f16_to_f32(brow[c]);
+    }
+    for (int64_t r = 0; r < nr; ++r) {
+      float* arow = acc + r * w;
+      const uint16_t* asrc = j->A + (j->r0 + r) * j->lda + k0;
+      for (int64_t kk = 0; kk < kn; ++kk) {
+        const float a = oracle_f16_to_f32(asrc[kk]);
+        const float* b = bf + kk * w;
+        /* k ascends for every element: the reference's accumulation order */
+        for (int64_t c = 0; c < w; ++c) arow[c] += a * b[c];
+      }
+    }
+  }
+  for (int64_t r = 0; r < nr; ++r) {
+    uint16_t* crow = j->C + (j->r0 + r) * j->ldc + j->c0;
+    for (int64_t c = 0; c < w; ++c) crow[c] = oracle_f32_to_f16(acc[r * w + c]);
+  }
+  free(acc);
+  free(bf);
+  return NULL;
+}
+
+/*
+ * C[M,N] = A[M,K] * B[K,N], fp16 bits in/out, row-major with pitches.
+ * Work is split over `nthreads` POSIX threads by column slices (rows when N
+ * is narrow).  Returns 0 on success.
+ */
+int oracle_gemm_f16(const uint16_t* A, const uint16_t* B, uint16_t* C, int64_t M, int64_t N, int64_t K,
+                    int64_t lda, int64_t ldb, int64_t ldc, int nthreads) {
+  if (M < 0 || N < 0 || K < 0) return 1;
+  if (M == 0 || N == 0) return 0;
+  if (nthreads < 1) nthreads = 1;
+  if (nthreads > 256) nthreads = 256;
+  oracle_job jobs[256];
+  pthread_t tids[256];
+  int started[256];
+  /* split the larger of (rows, column blocks of 64) */
+  const int64_t cblocks = (N + 63) / 64;
+  const int by_cols = cblocks >= nthreads || cblocks >= M;
+  int nj = 0;
+  for (int t = 0; t < nthreads; ++t) {
+    oracle_job j;
+    j.A = A;
+    j.B = B;
+    j.C = C;
+    j.M = M;
+    j.N = N;
+    j.K = K;
+    j.lda = lda;
+    j.ldb = ldb;
+    j.ldc = ldc;
+    if (by_cols) {
+      const int64_t b0 = cblocks * t / nthreads, b1 = cblocks * (t + 1) / nthreads;
+      j.r0 = 0;
+      j.r1 = M;
+      j.c0 = b0 * 64;
+      j.c1 = b1 * 64 < N ? b1 * 64 : N;
+    } else {
+      j.r0 = M * t / nthreads;
+      j.r1 = M * (t + 1) / nthreads;
+      j.c0 = 0;
+      j.c1 = N;
+    }
+    jobs[nj++] = j;
+  }
+  int rc = 0;
+  for (int t = 0; t < nj; ++t) {
+    started[t] = (nj > 1) && pthread_create(&tids[t], NULL, oracle_worker, &jobs[t]) == 0;
+    if (!started[t] && oracle_worker(&jobs[t]) != NULL) rc = 2;
+  }
+  for (int t = 0; t < nj; ++t) {
+    if (started[t]) {
+      void* ret = NULL;
+      pthread_join(tids[t], &ret);
+      if (ret != NULL) rc = 2;
+    }
+  }
+  return rc;
+}
