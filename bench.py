@@ -1,0 +1,402 @@
+"""Benchmark of the FP16 GEMM kernel bank (one JSON line on rank 0).
+
+Workload (every N): C[16384,16384] = A[16384,16384] * B[16384,16384], fp16 in,
+fp32 accumulate, fp16 out, A and B uniform[-1,1] from a seed.  A is split into
+N contiguous row blocks, one per rank (one process per GPU); B is generated on
+rank 0 and broadcast once at set-up (untimed); each rank computes its C rows
+with no data-path collective.  Total work is fixed, so scaling is "strong".
+A "step" is one GEMM over the local row block.  The optional NCCL all-gather
+of C (``--allgather``) is timed separately and reported under "allgather".
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  torchrun --nproc-per-node N bench.py --gpus N ...
+
+``--impl reference`` times the CPU restatement of the reference kernel (the
+oracle) on the host cores over a bounded sample of rows of the same workload;
+under torchrun only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+from typing import Dict, List, Optional
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "infinite-dreams_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "FP16 GEMM TFLOP/s and % of dense FP16 tensor peak per shape, 1/2/4/8 B200"
+NOMINAL_FP16_TFLOPS = 2250.0
+NOMINAL_HBM_GBS = 8000.0
+FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0}
+SIZE = 16384
+
+
+def parse() -> argparse.Namespace:
+    ap = argparse.ArgumentParser(description="FP16 GEMM kernel bank benchmark")
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--size", type=int, default=SIZE, help="M = N = K of the workload")
+    ap.add_argument("--cfg", type=int, default=None, help="menu cfg_id (default: dispatch table / heuristic)")
+    ap.add_argument("--allgather", action="store_true", help="also time the NCCL all-gather of C")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
+    return ap.parse_args()
+
+
+def peaks() -> Dict[str, object]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"bf16_tflops": float(d["bf16_tflops"]), "bf16_tflops_sustained": float(d["bf16_tflops_sustained"]),
+                "hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return dict(FALLBACK_PEAKS, source="fallback")
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples nvidia-smi clocks / throttle reasons in the background."""
+
+    FIELDS = ["index", "clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.active",
+              "clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
+              "clocks_event_reasons.sw_thermal_slowdown", "clocks_event_reasons.sw_power_cap"]
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.rows: List[List[str]] = []
+        self.proc: Optional[subprocess.Popen] = None
+        self.thread: Optional[threading.Thread] = None
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", "--query-gpu=" + ",".join(self.FIELDS),
+                 "--format=csv,noheader,nounits", "-lms", "20"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self) -> None:
+        assert self.proc is not None and self.proc.stdout is not None
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) == len(self.FIELDS):
+                self.rows.append(parts)
+
+    def stop(self) -> Dict[str, object]:
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+
+        def num(x: str) -> Optional[float]:
+            try:
+                return float(x)
+            except ValueError:
+                return None
+
+        power = [num(r[3]) or 0.0 for r in self.rows]
+        pmax = max(power)
+        loaded = [r for r, pw in zip(self.rows, power) if pw >= 0.5 * pmax] or self.rows
+        sm = [num(r[1]) for r in loaded if num(r[1]) is not None]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in loaded:
+            for name, v in zip(names, r[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": num(loaded[0][2]),
+                "reasons": sorted(reasons), "samples": len(loaded), "power_w_max": pmax}
+
+
+# ----------------------------------------------------------------------------- CPU oracle timing
+def cpu_oracle_sample(size: int, budget_s: float, seed: int = 0) -> Dict[str, object]:
+    """Times the oracle (CPU restatement of the reference kernel) on R rows of
+    the size^3 workload, R grown until the run takes about budget_s seconds."""
+    import numpy as np
+
+    import oracle
+
+    threads = len(os.sched_getaffinity(0))
+    rng = np.random.default_rng(seed)
+    B = rng.uniform(-1.0, 1.0, size=(size, size)).astype(np.float16)
+    def run(r: int) -> float:
+        A = rng.uniform(-1.0, 1.0, size=(r, size)).astype(np.float16)
+        t0 = time.perf_counter()
+        oracle.gemm_f16(A, B, threads=threads)
+        return time.perf_counter() - t0
+
+    # time(r) = fixed + r * per_row (the fixed part converts B once per call):
+    # fit both from two probes, then spend the budget on one timed sample.
+    t1, t2 = run(threads), run(4 * threads)
+    per_row = max((t2 - t1) / (3 * threads), 1e-9)
+    fixed = max(t1 - threads * per_row, 0.0)
+    total_rows = int(min(size, max(threads, (budget_s - fixed) / per_row)))
+    total_s = run(total_rows)
+    flops = 2.0 * total_rows * size * size
+    return {"value": flops / total_s / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{total_rows} rows of the {size}^3 GEMM ({flops / 1e9:.1f} GFLOP, {total_s:.1f} s)"}
+
+
+def run_reference(args: argparse.Namespace) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+
+    import oracle
+
+    size = args.size
+    threads = len(os.sched_getaffinity(0))
+    rng = np.random.default_rng(0)
+    B = rng.uniform(-1.0, 1.0, size=(size, size)).astype(np.float16)
+    # Size one step to ~1.5 s of host work so the whole run stays within minutes.
+    probe = rng.uniform(-1.0, 1.0, size=(4, size)).astype(np.float16)
+    t0 = time.perf_counter()
+    oracle.gemm_f16(probe, B, threads=threads)
+    per_row = (time.perf_counter() - t0) / 4
+    rows = int(max(1, min(size, 1.5 / max(per_row, 1e-9))))
+    A = rng.uniform(-1.0, 1.0, size=(rows, size)).astype(np.float16)
+    for _ in range(args.warmup):
+        oracle.gemm_f16(A, B, threads=threads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        oracle.gemm_f16(A, B, threads=threads)
+        times.append(time.perf_counter() - t0)
+    sec = sum(times) / len(times)
+    flops = 2.0 * rows * size * size
+    value = flops / sec / 1e12
+    sample = f"{rows} rows of the {size}^3 GEMM per step ({flops / 1e9:.1f} GFLOP)"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": workload_config(size, args.gpus, None),
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": ("the reference's path is a CUDA kernel with no CPU implementation; this arm times the "
+                 "oracle, a C restatement of that kernel's arithmetic (bit-exact to it), on the host cores"),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(size: int, n: int, knobs: Optional[Dict[str, int]]) -> Dict[str, object]:
+    cfg = {"workload": f"gemm {size}x{size}x{size} fp16 (fp32 accumulate), A row-sharded over {n} rank(s), "
+                       f"B replicated",
+           "M": size, "N": size, "K": size, "rows_per_rank": size // n, "inputs": "uniform[-1,1], seeded",
+           "parallelism": f"M-row shards x{n}, no data-path collective",
+           "l2": "inputs larger than L2 (A block >= 64 MiB, B 512 MiB): no flush needed"}
+    if knobs is not None:
+        cfg["kernel_cfg"] = knobs
+    return cfg
+
+
+# ----------------------------------------------------------------------------- our arm
+def run_ours(args: argparse.Namespace) -> None:
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    from infinite_dreams import dispatch, infinite_dreams_ext as ext
+
+    size = args.size
+    assert size % world == 0, "size must divide by the number of ranks"
+    rows = size // world
+    M, N, K = rows, size, size
+    cfg_id = args.cfg if args.cfg is not None else dispatch.lookup(M, N, K)
+    knobs = dict(zip(ext.CFG_COLUMNS, ext.gemm_cfg_table_cpu()[cfg_id].tolist()))
+
+    # inputs: rank r's A block comes from the seed (0, r); B from rank 0, broadcast
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    A = torch.rand((M, K), generator=g, device=dev, dtype=torch.float32).mul_(2).sub_(1).to(torch.float16)
+    if rank == 0:
+        g.manual_seed(7)
+        B = torch.rand((K, N), generator=g, device=dev, dtype=torch.float32).mul_(2).sub_(1).to(torch.float16)
+    else:
+        B = torch.empty((K, N), device=dev, dtype=torch.float16)
+    if world > 1:
+        dist.broadcast(B, src=0)
+    C = torch.empty((M, N), device=dev, dtype=torch.float16)
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        ext.gemm_forward_cfg(A, B, cfg_id, out=C)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    for _ in range(max(args.warmup, 3)):
+        step()
+    barrier()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for s, e in ev:
+        s.record(stream)
+        step()
+        e.record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    ms_local = t_start.elapsed_time(t_end)
+    kern_ms_local = sum(s.elapsed_time(e) for s, e in ev) / len(ev)
+    tvals = torch.tensor([ms_local, kern_ms_local], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(tvals, op=dist.ReduceOp.MAX)
+    ms_total, kern_ms = float(tvals[0]), float(tvals[1])
+    flops_total = 2.0 * size * size * size * args.steps
+    value = flops_total / (ms_total * 1e-3) / 1e12
+    ms_per_step = ms_total / args.steps
+
+    ext.check_device_errors(local)
+
+    # optional all-gather of C row blocks (NCCL over NVLink), timed on its own
+    allgather = None
+    if world > 1 and args.allgather:
+        Cfull = torch.empty((size, N), device=dev, dtype=torch.float16)
+        for _ in range(2):
+            dist.all_gather_into_tensor(Cfull, C)
+        barrier()
+        s0 = torch.cuda.Event(enable_timing=True)
+        s1 = torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for _ in range(args.steps):
+            step()
+            dist.all_gather_into_tensor(Cfull, C)
+        s1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([s0.elapsed_time(s1)], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_ag = float(t[0]) / args.steps
+        allgather = {"ms_per_step_gemm_plus_allgather": ms_ag,
+                     "value_with_allgather": 2.0 * size ** 3 / (ms_ag * 1e-3) / 1e12,
+                     "bytes_received_per_rank": (world - 1) * rows * N * 2}
+        del Cfull
+
+    # end to end through the public op: pinned host -> device, GEMM, device -> host
+    e2e = None
+    if not args.no_e2e:
+        hA = A.cpu().pin_memory()
+        hB = B.cpu().pin_memory()
+        hC = torch.empty((M, N), dtype=torch.float16).pin_memory()
+        dA = torch.empty_like(A)
+        dB = torch.empty_like(B)
+        e2e_steps = max(1, min(args.steps, 10))
+
+        def e2e_step():
+            dA.copy_(hA, non_blocking=True)
+            dB.copy_(hB, non_blocking=True)
+            ext.gemm_forward_cfg(dA, dB, cfg_id, out=C)
+            hC.copy_(C, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        barrier()
+        s0 = torch.cuda.Event(enable_timing=True)
+        s1 = torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        s1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([s0.elapsed_time(s1)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_e2e = float(t[0]) / e2e_steps
+        e2e = {"value": 2.0 * size ** 3 / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": (M * K + K * N) * 2 * world, "d2h_bytes_per_step": M * N * 2 * world,
+               "ms_per_step": ms_e2e, "steps": e2e_steps,
+               "path": "pinned host A,B -> device, infinite_dreams_ext.gemm_forward_cfg, C -> pinned host"}
+        del hA, hB, hC, dA, dB
+
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    pk = peaks()
+    peak = float(pk["bf16_tflops"])
+    achieved = 2.0 * M * N * K / (kern_ms * 1e-3) / 1e12
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak, "peak_source": f"{pk['source']} bf16 dense burst",
+                "frac_of_nominal_2250": achieved / NOMINAL_FP16_TFLOPS,
+                "kernel": f"gemm_f16_sm100<{knobs['tile_n']},{knobs['stages']}>",
+                "algorithmic_flop_per_launch": 2.0 * M * N * K, "launch_ms": kern_ms,
+                "traffic": traffic_for(size, world)}
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_oracle_sample(size, args.cpu_seconds)
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": workload_config(size, world, knobs),
+        "pct_of_dense_fp16_peak": 100.0 * value / (NOMINAL_FP16_TFLOPS * world),
+        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps,
+        "clocks": clocks, "allgather": allgather,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def traffic_for(size: int, world: int) -> Optional[float]:
+    """DRAM bytes per launch from the committed ncu summary, if one covers this case."""
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    if not p.exists():
+        return None
+    try:
+        d = json.loads(p.read_text())
+        return d.get(f"{size}x{world}")
+    except (ValueError, OSError):
+        return None
+
+
+def main() -> None:
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

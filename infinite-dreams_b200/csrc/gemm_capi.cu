@@ -237,7 +237,7 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
   if (M < 0 || N < 0 || K < 0) return fail(GEMM_ERR_INVALID_ARG, "M, N, K must be >= 0");
   if (M == 0 || N == 0) return GEMM_OK;
-  if (!A || !B || !C) return fail(GEMM_ERR_INVALID_ARG, "A, B and C must be non-null");
+  if (!C || (K > 0 && (!A || !B))) return fail(GEMM_ERR_INVALID_ARG, "A, B and C must be non-null");
   if (lda < K || ldb < N || ldc < N) {
     return fail(GEMM_ERR_INVALID_ARG, "pitches must satisfy lda >= K, ldb >= N, ldc >= N");
   }

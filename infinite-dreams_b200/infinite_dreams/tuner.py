@@ -1,0 +1,412 @@
+"""Discrete differential-evolution tuner over the sm_100a kernel-bank menu.
+
+Restates the reference tuner (infinite_dreams/tuner.py) on the Blackwell
+knob space and fixes its defects:
+
+* same algorithm: DE/rand/1/bin (mutant ``va + F*(vb - vc)``, binomial
+  crossover with a forced ``jrand`` gene, clipping, greedy replacement;
+  tuner.py:316-417), continuous genes quantised to the knob grid
+  (tuner.py:157-174) and projected onto the menu by best-first search
+  (``project_to_valid``, tuner.py:78-122), fitness = mean device ms over the
+  benchmark shapes, cached per tuple and logged per evaluation
+  (``TileScorer``, tuner.py:183-313), then a confirmation re-rank of the
+  top-k (``rerank_topk``, tuner.py:420-457);
+* genes are indices into each knob's value list (tile_m, tile_n, tile_k,
+  stages, mma_sm, raster, group, split_k) instead of raw tile sizes;
+* the RNG is seeded (``--seed``; the reference used an unseeded
+  ``default_rng()`` and read an undeclared ``args.seed``, tuner.py:325,499);
+* timing uses distinct start/stop events (the reference aliased one event,
+  utils.py:19) and can flush L2 between repetitions;
+* ``--per-shape`` tunes every shape of a set separately and persists the
+  winner to the dispatch table (``dispatch.py``).
+
+Usage: ``python -m infinite_dreams.tuner [--pop 50 --gen 20 --F 0.7 --CR 0.9 ...]``
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import heapq
+import os
+import time
+from dataclasses import dataclass
+from typing import Any, Callable, Dict, List, Optional, Sequence, Set, Tuple
+
+import numpy as np
+
+from .gen_gemm_bank import COLUMNS, GROUPS, MMA_SMS, RASTERS, SPLIT_KS, STAGES, TILE_KS, TILE_MS, TILE_NS, \
+    enumerate_menu
+
+Knobs = Tuple[int, ...]
+
+# Value grid of every gene (sorted), in menu column order.
+CHOICES: Tuple[Tuple[int, ...], ...] = (TILE_MS, TILE_NS, TILE_KS, STAGES, MMA_SMS, RASTERS, GROUPS, SPLIT_KS)
+NDIM = len(CHOICES)
+
+
+class Menu:
+    """The kernel-bank menu: knob tuple <-> cfg_id.
+
+    By default it comes from the compiled library (``gemm_cfg_table_cpu``),
+    as the reference read its menu from the extension (tuner.py:21-27); the
+    generator's enumeration (identical by construction) serves CPU-only use.
+    """
+
+    def __init__(self, rows: Optional[Sequence[Knobs]] = None):
+        if rows is None:
+            rows = [tuple(r) for r in enumerate_menu()]
+        self.rows: List[Knobs] = [tuple(int(v) for v in r) for r in rows]
+        self.index: Dict[Knobs, int] = {r: i for i, r in enumerate(self.rows)}
+
+    @classmethod
+    def from_library(cls) -> "Menu":
+        from . import _capi
+        return cls(_capi.menu()[1])
+
+    def __len__(self) -> int:
+        return len(self.rows)
+
+    def cfg_to_id(self, knobs: Knobs) -> int:
+        return self.index.get(tuple(knobs), -1)
+
+
+@dataclass(frozen=True)
+class TileConfig:
+    tile_m: int
+    tile_n: int
+    tile_k: int
+    stages: int
+    mma_sm: int
+    raster: int
+    group: int
+    split_k: int
+
+    def as_tuple(self) -> Knobs:
+        return (self.tile_m, self.tile_n, self.tile_k, self.stages, self.mma_sm, self.raster, self.group,
+                self.split_k)
+
+
+def to_indices(knobs: Knobs) -> Tuple[int, ...]:
+    return tuple(CHOICES[d].index(v) if v in CHOICES[d] else 0 for d, v in enumerate(knobs))
+
+
+def from_indices(idx: Sequence[int]) -> Knobs:
+    return tuple(CHOICES[d][int(i)] for d, i in enumerate(idx))
+
+
+# Weights of the projection distance: changing the tile shape hurts most,
+# split-K and pipeline depth less, raster/group least (cf. tuner.py:55-75).
+_WEIGHTS = (3, 3, 3, 2, 3, 1, 1, 2)
+
+
+def _score(orig: Sequence[int], cand: Sequence[int], cand_knobs: Knobs) -> Tuple[int, int, int]:
+    dist = sum(w * abs(a - b) for w, a, b in zip(_WEIGHTS, orig, cand))
+    # prefer a larger output tile, then deeper pipelines (throughput potential)
+    return dist, -(cand_knobs[0] * cand_knobs[1]), -cand_knobs[3]
+
+
+def project_to_valid(cfg: TileConfig, menu: Menu, budget: int = 100000) -> TileConfig:
+    """Nearest menu member by best-first search over +-1 index moves."""
+    if menu.cfg_to_id(cfg.as_tuple()) >= 0:
+        return cfg
+    start = to_indices(cfg.as_tuple())
+    pq: List[Tuple[Tuple[int, int, int], Tuple[int, ...]]] = []
+    seen: Set[Tuple[int, ...]] = set()
+
+    def push(state: Tuple[int, ...]) -> None:
+        if state in seen:
+            return
+        seen.add(state)
+        heapq.heappush(pq, (_score(start, state, from_indices(state)), state))
+
+    push(start)
+    while pq and len(seen) <= budget:
+        _, cur = heapq.heappop(pq)
+        knobs = from_indices(cur)
+        if menu.cfg_to_id(knobs) >= 0:
+            return TileConfig(*knobs)
+        for d in range(NDIM):
+            for step in (-1, 1):
+                v = cur[d] + step
+                if 0 <= v < len(CHOICES[d]):
+                    push(cur[:d] + (v,) + cur[d + 1:])
+    raise RuntimeError(f"no menu member near {cfg}")
+
+
+def quantize_index(x: float, n: int) -> int:
+    """Nearest grid index in [0, n-1]; ties go to the smaller index (cf. tuner.py:166-174)."""
+    v = int(np.floor(x + 0.5)) if x - np.floor(x) != 0.5 else int(np.floor(x))
+    return min(max(v, 0), n - 1)
+
+
+@dataclass(frozen=True)
+class BenchCase:
+    M: int
+    N: int
+    K: int
+    A: Any
+    B: Any
+
+
+def make_bench_cases(sizes: Sequence[Tuple[int, int, int]], seed: Optional[int] = 0, device: str = "cuda",
+                     dist: str = "uniform") -> List[BenchCase]:
+    """Pre-allocated seeded fp16 inputs (uniform[-1,1] or N(0,1) x N(0,0.02^2))."""
+    import torch
+
+    g = torch.Generator(device=device)
+    g.manual_seed(0 if seed is None else int(seed))
+    cases = []
+    for (M, N, K) in sizes:
+        if dist == "skinny":
+            A = torch.randn((M, K), device=device, generator=g, dtype=torch.float32).to(torch.float16)
+            B = (torch.randn((K, N), device=device, generator=g, dtype=torch.float32) * 0.02).to(torch.float16)
+        else:
+            A = (torch.rand((M, K), device=device, generator=g, dtype=torch.float32) * 2 - 1).to(torch.float16)
+            B = (torch.rand((K, N), device=device, generator=g, dtype=torch.float32) * 2 - 1).to(torch.float16)
+        cases.append(BenchCase(M=M, N=N, K=K, A=A, B=B))
+    return cases
+
+
+@dataclass
+class ScoreOptions:
+    iters: int
+    warmup: int
+    flush_l2: bool = False
+
+
+EVAL_FIELDS = ["eval_id", "timestamp_ms", "phase", "gen", "pop_i", "cfg_id", *COLUMNS, "ms", "tflops",
+               "cache_hit", "valid_cfg", "shapes"]
+
+
+class TileScorer:
+    """Benchmarks configs on pre-allocated inputs; caches per knob tuple and
+    logs every evaluation (the reference's eval-log schema, tuner.py:214-229,
+    with the Blackwell knob columns and TFLOP/s)."""
+
+    INVALID_MS = 1e9
+
+    def __init__(self, cases: Sequence[BenchCase], score_opts: ScoreOptions, menu: Menu,
+                 eval_log_path: Optional[str] = None,
+                 measure: Optional[Callable[[int, BenchCase, ScoreOptions], float]] = None):
+        self.cases = list(cases)
+        self.opts = score_opts
+        self.menu = menu
+        self.cache: Dict[Knobs, float] = {}
+        self.measure = measure or _measure_cuda
+        self.eval_log_path = eval_log_path
+        self._eval_id = 0
+        self._csv_file = None
+        self._csv_writer = None
+        self.phase, self.gen, self.pop_i = "unknown", -1, -1
+        flops = [2.0 * c.M * c.N * c.K for c in self.cases]
+        self._mean_flops = float(np.mean(flops)) if flops else 0.0
+        if eval_log_path is not None:
+            os.makedirs(os.path.dirname(eval_log_path) or ".", exist_ok=True)
+            new_file = not os.path.exists(eval_log_path)
+            self._csv_file = open(eval_log_path, "a", newline="")
+            self._csv_writer = csv.DictWriter(self._csv_file, fieldnames=EVAL_FIELDS)
+            if new_file:
+                self._csv_writer.writeheader()
+                self._csv_file.flush()
+
+    def set_context(self, phase: str, gen: int, pop_i: int) -> None:
+        self.phase, self.gen, self.pop_i = phase, int(gen), int(pop_i)
+
+    def _log(self, knobs: Knobs, cfg_id: int, ms: float, cache_hit: int, valid: int) -> None:
+        if self._csv_writer is None:
+            return
+        row = dict(eval_id=self._eval_id, timestamp_ms=int(time.time() * 1000), phase=self.phase, gen=self.gen,
+                   pop_i=self.pop_i, cfg_id=cfg_id, ms=float(ms),
+                   tflops=(self._mean_flops / (ms * 1e-3) / 1e12) if valid and ms > 0 else 0.0,
+                   cache_hit=int(cache_hit), valid_cfg=int(valid),
+                   shapes=";".join(f"{c.M}x{c.N}x{c.K}" for c in self.cases))
+        row.update(dict(zip(COLUMNS, knobs)))
+        self._csv_writer.writerow(row)
+        self._csv_file.flush()
+        self._eval_id += 1
+
+    def close(self) -> None:
+        if self._csv_file is not None:
+            self._csv_file.close()
+            self._csv_file = None
+            self._csv_writer = None
+
+    def score(self, cfg: TileConfig) -> float:
+        key = cfg.as_tuple()
+        cfg_id = self.menu.cfg_to_id(key)
+        if key in self.cache:
+            self._log(key, cfg_id, self.cache[key], 1, int(cfg_id >= 0))
+            return self.cache[key]
+        if cfg_id < 0:
+            self.cache[key] = self.INVALID_MS
+            self._log(key, cfg_id, self.INVALID_MS, 0, 0)
+            return self.INVALID_MS
+        ms = float(np.mean([self.measure(cfg_id, c, self.opts) for c in self.cases]))
+        self.cache[key] = ms
+        self._log(key, cfg_id, ms, 0, 1)
+        return ms
+
+
+def _measure_cuda(cfg_id: int, case: BenchCase, opts: ScoreOptions) -> float:
+    import torch
+
+    from . import infinite_dreams_ext as ext
+    from .utils import time_cuda_ms
+
+    out = torch.empty((case.M, case.N), dtype=torch.float16, device=case.A.device)
+    return time_cuda_ms(lambda: ext.gemm_forward_cfg(case.A, case.B, cfg_id, out=out), iters=opts.iters,
+                        warmup=opts.warmup, flush_l2=opts.flush_l2)
+
+
+def differential_evolution_discrete(pop_size: int, generations: int, F: float, CR: float, scorer: TileScorer,
+                                    seed: Optional[int] = 0, verbose: bool = True,
+                                    fixed: Optional[Dict[int, int]] = None
+                                    ) -> Tuple[TileConfig, float, List[Dict[str, Any]]]:
+    """DE/rand/1/bin over gene indices; returns (best config, its ms, history rows)."""
+    rng = np.random.default_rng(seed)
+    hi = np.array([len(c) - 1 for c in CHOICES], dtype=np.float64)
+    fixed = fixed or {}
+    if pop_size < 4:
+        raise ValueError("DE/rand/1 needs pop_size >= 4")
+
+    def rand_vec() -> np.ndarray:
+        v = rng.uniform(0.0, 1.0, size=NDIM) * hi
+        for d, i in fixed.items():
+            v[d] = i
+        return v
+
+    def vec_to_cfg(v: np.ndarray) -> TileConfig:
+        idx = [quantize_index(float(v[d]), len(CHOICES[d])) for d in range(NDIM)]
+        return project_to_valid(TileConfig(*from_indices(idx)), scorer.menu)
+
+    pop = [rand_vec() for _ in range(pop_size)]
+    scores = np.empty(pop_size, dtype=np.float64)
+    for i, v in enumerate(pop):
+        scorer.set_context("search_init", -1, i)
+        scores[i] = scorer.score(vec_to_cfg(v))
+    history: List[Dict[str, Any]] = []
+    best_i = int(np.argmin(scores))
+    for gen in range(generations):
+        for i in range(pop_size):
+            idxs = [j for j in range(pop_size) if j != i]
+            a, b, c = rng.choice(idxs, size=3, replace=False)
+            mutant = pop[a] + F * (pop[b] - pop[c])
+            trial = pop[i].copy()
+            jrand = int(rng.integers(0, NDIM))
+            for j in range(NDIM):
+                if rng.random() < CR or j == jrand:
+                    trial[j] = mutant[j]
+            trial = np.clip(trial, 0.0, hi)
+            for d, fi in fixed.items():
+                trial[d] = fi
+            scorer.set_context("search", gen, i)
+            s = scorer.score(vec_to_cfg(trial))
+            if s < scores[i]:
+                pop[i] = trial
+                scores[i] = s
+        best_i = int(np.argmin(scores))
+        best_cfg = vec_to_cfg(pop[best_i])
+        row = dict(phase="search", gen=gen, ms=float(scores[best_i]), cfg_id=scorer.menu.cfg_to_id(best_cfg.as_tuple()))
+        row.update(dict(zip(COLUMNS, best_cfg.as_tuple())))
+        history.append(row)
+        if verbose:
+            print(f"[gen {gen:03d}] best ms={scores[best_i]:.4f} cfg_id={row['cfg_id']} cfg={best_cfg}", flush=True)
+    final = vec_to_cfg(pop[best_i])
+    return final, scorer.score(final), history
+
+
+def rerank_topk(candidates: Sequence[TileConfig], scorer: TileScorer) -> Tuple[List[Tuple[TileConfig, float]],
+                                                                               List[Dict[str, Any]]]:
+    """Re-benchmarks candidates with the scorer's (longer) options; best first."""
+    scored, rows = [], []
+    for rank, cfg in enumerate(candidates):
+        scorer.set_context("confirm", -1, rank)
+        ms = scorer.score(cfg)
+        scored.append((cfg, ms))
+        row = dict(phase="confirm", rank=rank, ms=ms, cfg_id=scorer.menu.cfg_to_id(cfg.as_tuple()))
+        row.update(dict(zip(COLUMNS, cfg.as_tuple())))
+        rows.append(row)
+    scored.sort(key=lambda x: x[1])
+    return scored, rows
+
+
+def tune(sizes: Sequence[Tuple[int, int, int]], args: argparse.Namespace, menu: Menu,
+         dist: str = "uniform") -> Tuple[TileConfig, float, List[Dict[str, Any]]]:
+    cases = make_bench_cases(sizes, seed=args.seed, dist=dist)
+    flush = args.flush_l2 or all(2 * (c.M * c.K + c.K * c.N + c.M * c.N) < 96 * 2 ** 20 for c in cases)
+    scorer = TileScorer(cases, ScoreOptions(args.search_iters, args.search_warmup, flush), menu,
+                        eval_log_path=args.eval_log)
+    best, best_ms, hist = differential_evolution_discrete(args.pop, args.gen, args.F, args.CR, scorer,
+                                                          seed=args.seed, verbose=not args.quiet)
+    top = [TileConfig(*k) for k, v in sorted(scorer.cache.items(), key=lambda kv: kv[1])
+           if v < TileScorer.INVALID_MS][: args.topk]
+    confirm = TileScorer(cases, ScoreOptions(args.confirm_iters, args.confirm_warmup, flush), menu,
+                         eval_log_path=args.eval_log)
+    confirmed, rows = rerank_topk(top, confirm)
+    scorer.close()
+    confirm.close()
+    hist.extend(rows)
+    cfg, ms = confirmed[0]
+    best_row = dict(phase="best", ms=ms, cfg_id=menu.cfg_to_id(cfg.as_tuple()))
+    best_row.update(dict(zip(COLUMNS, cfg.as_tuple())))
+    hist.append(best_row)
+    return cfg, ms, hist
+
+
+def main(argv: Optional[Sequence[str]] = None) -> None:
+    from . import dispatch
+    from .sizes import shape_sets
+    from .utils import HISTORY_FIELDS, write_csv
+
+    ap = argparse.ArgumentParser(description="DE tuner over the sm_100a kernel-bank menu")
+    ap.add_argument("--pop", type=int, default=50)
+    ap.add_argument("--gen", type=int, default=20)
+    ap.add_argument("--F", type=float, default=0.7)
+    ap.add_argument("--CR", type=float, default=0.9)
+    ap.add_argument("--search-iters", type=int, default=10)
+    ap.add_argument("--search-warmup", type=int, default=2)
+    ap.add_argument("--topk", type=int, default=10)
+    ap.add_argument("--confirm-iters", type=int, default=100)
+    ap.add_argument("--confirm-warmup", type=int, default=20)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--shapes", default="default", help="shape set: " + ", ".join(shape_sets()))
+    ap.add_argument("--per-shape", action="store_true", help="tune each shape and persist the dispatch table")
+    ap.add_argument("--table", default=None, help="dispatch table path (default: package table)")
+    ap.add_argument("--flush-l2", action="store_true")
+    ap.add_argument("--out", type=str, default="results/tune_history.csv")
+    ap.add_argument("--eval-log", type=str, default="results/eval_log.csv")
+    ap.add_argument("--quiet", action="store_true")
+    args = ap.parse_args(argv)
+
+    import torch
+
+    menu = Menu.from_library()
+    sizes = shape_sets()[args.shapes]
+    dist = "skinny" if args.shapes == "skinny" else "uniform"
+    if args.eval_log and os.path.exists(args.eval_log):
+        os.remove(args.eval_log)
+    rows: List[Dict[str, Any]] = []
+    if args.per_shape:
+        for shape in sizes:
+            cfg, ms, hist = tune([shape], args, menu, dist)
+            for r in hist:
+                r["shape"] = "x".join(map(str, shape))
+            rows.extend(hist)
+            dispatch.save_entry(*shape, cfg.as_tuple(), ms, COLUMNS, path=args.table,
+                                device=torch.cuda.get_device_name())
+            if not args.quiet:
+                print(f"{shape}: {cfg} {ms:.4f} ms = {2 * np.prod(shape) / (ms * 1e-3) / 1e12:.1f} TFLOP/s",
+                      flush=True)
+    else:
+        cfg, ms, hist = tune(sizes, args, menu, dist)
+        rows.extend(hist)
+        if not args.quiet:
+            print(f"Menu size: {len(menu)} configs")
+            print(f"Confirm-best: {cfg} ms={ms:.4f} cfg_id={menu.cfg_to_id(cfg.as_tuple())}")
+    write_csv(args.out, rows, HISTORY_FIELDS + ["stages", "mma_sm", "raster", "group", "split_k", "shape"])
+    if not args.quiet:
+        print(f"Wrote: {args.out}")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,49 @@
+"""Generator: the Blackwell config space, its validity rules and its outputs."""
+import itertools
+
+from infinite_dreams import gen_gemm_bank as gen
+
+
+def test_menu_is_sorted_unique_and_valid():
+    menu = gen.enumerate_menu()
+    assert menu == sorted(set(menu))
+    assert len(menu) > 100
+    assert all(gen.valid(c) for c in menu)
+
+
+def test_valid_rules():
+    ok = (128, 256, 64, 4, 1, 0, 8, 1)
+    assert gen.valid(ok)
+    assert not gen.valid((128, 256, 64, 5, 1, 0, 8, 1))   # shared memory above 227 KiB
+    assert not gen.valid((128, 96, 64, 4, 1, 0, 8, 1))    # tile_n not a multiple of 64
+    assert not gen.valid((128, 320, 64, 2, 1, 0, 8, 1))   # MMA N above 256
+    assert not gen.valid((256, 128, 64, 4, 1, 0, 8, 1))   # tile_m must equal 128 * mma_sm
+    assert not gen.valid((128, 128, 32, 4, 1, 0, 8, 1))   # tile_k is one 128-byte swizzle row
+    assert not gen.valid((128, 128, 64, 1, 1, 0, 8, 1))   # at least double buffering
+    assert not gen.valid((128, 128, 64, 4, 1, 0, 0, 1))   # group >= 1
+    assert not gen.valid((128, 128, 64, 4, 1, 0, 8, 0))   # split_k >= 1
+
+
+def test_every_valid_combination_is_in_the_menu():
+    menu = set(gen.enumerate_menu())
+    for c in itertools.product(gen.TILE_MS, gen.TILE_NS, gen.TILE_KS, gen.STAGES, gen.MMA_SMS, gen.RASTERS,
+                               gen.GROUPS, gen.SPLIT_KS):
+        assert (c in menu) == gen.valid(c)
+
+
+def test_smem_fits_and_max_stages_per_tile():
+    menu = gen.enumerate_menu()
+    for bn, st in gen.variants(menu):
+        assert gen.smem_bytes(128, bn, 64, st) <= gen.SMEM_CAP
+        assert gen.tmem_cols(bn) <= 512
+    deepest = {bn: max(st for b, st in gen.variants(menu) if b == bn) for bn in gen.TILE_NS}
+    assert deepest == {64: 8, 128: 6, 192: 4, 256: 4}
+
+
+def test_generated_files_up_to_date():
+    assert gen.write(check=True) == [], "csrc/generated is stale: run gen_gemm_bank.py"
+
+
+def test_render_is_deterministic():
+    m = gen.enumerate_menu()
+    assert gen.render(m) == gen.render(list(m))
