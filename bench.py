@@ -169,12 +169,19 @@ def run_reference(args: argparse.Namespace) -> None:
     threads = len(os.sched_getaffinity(0))
     rng = np.random.default_rng(0)
     B = rng.uniform(-1.0, 1.0, size=(size, size)).astype(np.float16)
-    # Size one step to ~1.5 s of host work so the whole run stays within minutes.
-    probe = rng.uniform(-1.0, 1.0, size=(4, size)).astype(np.float16)
-    t0 = time.perf_counter()
-    oracle.gemm_f16(probe, B, threads=threads)
-    per_row = (time.perf_counter() - t0) / 4
-    rows = int(max(1, min(size, 1.5 / max(per_row, 1e-9))))
+    # Size one step so that the whole --steps/--warmup run takes ~90 s of host
+    # work: time(r) = fixed + r * per_row, fitted from two probes.
+    def run(r: int) -> float:
+        a = rng.uniform(-1.0, 1.0, size=(r, size)).astype(np.float16)
+        t0 = time.perf_counter()
+        oracle.gemm_f16(a, B, threads=threads)
+        return time.perf_counter() - t0
+
+    t1, t2 = run(threads), run(4 * threads)
+    per_row = max((t2 - t1) / (3 * threads), 1e-9)
+    fixed = max(t1 - threads * per_row, 0.0)
+    step_budget = max(0.2, 90.0 / max(1, args.steps + args.warmup))
+    rows = int(min(size, max(1, (step_budget - fixed) / per_row)))
     A = rng.uniform(-1.0, 1.0, size=(rows, size)).astype(np.float16)
     for _ in range(args.warmup):
         oracle.gemm_f16(A, B, threads=threads)

@@ -14,10 +14,11 @@ namespace idb {
 using LaunchFn = cudaError_t (*)(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c,
                                  const GemmParams& p, int grid, cudaStream_t stream);
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int CG>
 cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c, const GemmParams& p,
                         int grid, cudaStream_t stream) {
-  using Plan = SmemPlan<BN, STAGES>;
+  using Plan = SmemPlan<BN, STAGES, CG>;
+  auto kernel = gemm_f16_sm100<BN, STAGES, CG>;
   // The opt-in shared-memory size is a per-device function attribute.
   static std::atomic<unsigned long long> configured{0};
   int dev = 0;
@@ -25,19 +26,35 @@ cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtens
   if (e != cudaSuccess) return e;
   const unsigned long long bit = 1ull << (dev & 63);
   if (!(configured.load(std::memory_order_acquire) & bit)) {
-    e = cudaFuncSetAttribute(gemm_f16_sm100<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             Plan::kDynamicBytes);
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Plan::kDynamicBytes);
     if (e != cudaSuccess) return e;
     configured.fetch_or(bit, std::memory_order_acq_rel);
   }
-  gemm_f16_sm100<BN, STAGES><<<grid, kNumThreads, Plan::kDynamicBytes, stream>>>(a, b, c, p);
-  return cudaGetLastError();
+  if constexpr (CG == 1) {
+    kernel<<<grid, kNumThreads, Plan::kDynamicBytes, stream>>>(a, b, c, p);
+    return cudaGetLastError();
+  } else {
+    // CTA pairs: a cluster of 2 along x; grid is a multiple of 2.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+    cfg.blockDim = dim3(kNumThreads, 1, 1);
+    cfg.dynamicSmemBytes = Plan::kDynamicBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, a, b, c, p);
+  }
 }
 
 }  // namespace idb
 
-#define IDB_DEFINE_VARIANT(BN, ST)                                                                        \
-  cudaError_t launch_bn##BN##_s##ST(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c,   \
-                                    const GemmParams& p, int grid, cudaStream_t stream) {               \
-    return launch_gemm<BN, ST>(a, b, c, p, grid, stream);                                               \
+#define IDB_DEFINE_VARIANT(BN, ST, CG)                                                                    \
+  cudaError_t launch_bn##BN##_s##ST##_cg##CG(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c, \
+                                             const GemmParams& p, int grid, cudaStream_t stream) {        \
+    return launch_gemm<BN, ST, CG>(a, b, c, p, grid, stream);                                            \
   }

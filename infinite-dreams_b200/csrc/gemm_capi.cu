@@ -22,20 +22,21 @@
 
 namespace idb {
 
-#define IDB_VARIANT(BN, ST)                                                                              \
-  cudaError_t launch_bn##BN##_s##ST(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c,   \
-                                    const GemmParams& p, int grid, cudaStream_t stream);
+#define IDB_VARIANT(BN, ST, CG)                                                                           \
+  cudaError_t launch_bn##BN##_s##ST##_cg##CG(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c, \
+                                             const GemmParams& p, int grid, cudaStream_t stream);
 #include "generated/gemm_variants.inc"
 #undef IDB_VARIANT
 
 struct Variant {
   int bn;
   int stages;
+  int cg;
   LaunchFn fn;
 };
 
 static const Variant kVariants[] = {
-#define IDB_VARIANT(BN, ST) {BN, ST, &launch_bn##BN##_s##ST},
+#define IDB_VARIANT(BN, ST, CG) {BN, ST, CG, &launch_bn##BN##_s##ST##_cg##CG},
 #include "generated/gemm_variants.inc"
 #undef IDB_VARIANT
 };
@@ -139,7 +140,7 @@ bool tma_addressable(const void* p, int64_t pitch_elems) {
 int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 
 struct Plan {
-  int tile_n = 0, stages = 0, raster = 0, group = 1, split_k = 1;
+  int tile_m = 0, tile_n = 0, stages = 0, cg = 1, raster = 0, group = 1, split_k = 1;
   int tiles_m = 0, tiles_n = 0, num_tiles = 0, kb_total = 0;
   bool pack_a = false, pack_b = false;
   size_t off_partials = 0, off_pack_a = 0, off_pack_b = 0, total = 0;
@@ -159,11 +160,13 @@ int make_plan(const void* A, const void* B, int64_t M, int64_t N, int64_t K, int
     return fail(GEMM_ERR_UNSUPPORTED, "M, N, K must each be < 2^31");
   }
   const int* row = kMenu[cfg_id];
+  pl->tile_m = row[kColTileM];
   pl->tile_n = row[kColTileN];
+  pl->cg = row[kColMmaSm];
   pl->stages = row[kColStages];
   pl->raster = row[kColRaster];
   pl->group = row[kColGroup];
-  pl->tiles_m = static_cast<int>((M + kBM - 1) / kBM);
+  pl->tiles_m = static_cast<int>((M + pl->tile_m - 1) / pl->tile_m);
   pl->tiles_n = static_cast<int>((N + pl->tile_n - 1) / pl->tile_n);
   const int64_t tiles = static_cast<int64_t>(pl->tiles_m) * pl->tiles_n;
   if (tiles > (1ll << 30)) return fail(GEMM_ERR_UNSUPPORTED, "too many output tiles");
@@ -265,7 +268,7 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
   }
   const Variant* var = nullptr;
   for (const Variant& v : kVariants) {
-    if (v.bn == pl.tile_n && v.stages == pl.stages) var = &v;
+    if (v.bn == pl.tile_n && v.stages == pl.stages && v.cg == pl.cg) var = &v;
   }
   if (!var) return fail(GEMM_ERR_BAD_CFG, "no compiled kernel for this configuration");
 
@@ -322,7 +325,9 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
   p.err = err_word;
 
   const int64_t units = static_cast<int64_t>(pl.num_tiles) * pl.split_k;
-  const int grid = static_cast<int>(units < dinfo.sms ? units : dinfo.sms);
+  // persistent grid: one CTA (or CTA pair) per SM (pair), at most one per work unit
+  const int64_t slots = dinfo.sms / pl.cg;
+  const int grid = static_cast<int>((units < slots ? units : slots) * pl.cg);
   e = var->fn(tmA, tmB, tmC, p, grid, stream);
   if (e != cudaSuccess) return fail_cuda(e, "gemm kernel launch");
   return GEMM_OK;
@@ -398,9 +403,18 @@ int gemm_launch_knobs(const void* A, const void* B, void* C, int64_t M, int64_t 
 }
 
 int gemm_default_cfg(int64_t M, int64_t N, int64_t K) {
-  // Heuristic: the widest tile whose wave count is reasonable; split K when
-  // the output has too few tiles to occupy the 148 SMs.
+  // Heuristic used when no tuned entry exists:
+  //  * enough 256 x 256 tiles to fill the 74 CTA pairs of a B200: CTA-pair
+  //    (cta_group::2) kernel, 4 stages;
+  //  * otherwise one CTA per 128-row tile, the widest tile_n that still
+  //    gives ~one wave, and split-K when the output has too few tiles to
+  //    occupy the 148 SMs.
   const int kSms = 148;
+  const int64_t pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
+  if (pair_tiles >= kSms / 2) {
+    int knobs[IDB_MENU_COLS] = {2 * kBM, 256, kBK, 4, 2, 0, 8, 1};
+    return gemm_cfg_find(knobs, IDB_MENU_COLS);
+  }
   int tile_n = 256, stages = 4;
   const int64_t tm = (M + kBM - 1) / kBM;
   if (tm * ((N + 255) / 256) < kSms) {

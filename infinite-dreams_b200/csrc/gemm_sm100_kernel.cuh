@@ -9,7 +9,7 @@
 //               B boxes [64 x 64] (N-major, 128B swizzle) per pipeline stage,
 //               completing on a `full` mbarrier.
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
-//               (M=128, N=BN, K=16 per instruction), frees smem stages with
+//               (K=16 per instruction), frees smem stages with
 //               tcgen05.commit -> `empty` mbarrier, hands finished accumulators
 //               to the epilogue with tcgen05.commit -> `tmem_full`.
 //   warps 2..5  epilogue: tcgen05.ld (32 lanes x 32 columns per warp), fp16
@@ -18,6 +18,14 @@
 //               aligned).  Split-K partials go to an fp32 workspace; the last
 //               CTA of a tile (atomic ticket, no spinning) sums the partials
 //               in split order and writes C.
+//
+// CG (CTA group) = 1: one CTA owns a 128 x BN tile (MMA M=128).
+// CG = 2: a cluster of two CTAs owns a 256 x BN tile (tcgen05 cta_group::2,
+// MMA M=256).  Each CTA loads its own 128 rows of A and its own BN/2 columns
+// of B (no multicast); the even CTA issues the MMAs, which read both CTAs'
+// shared memory and write each CTA's 128 accumulator rows into its own TMEM;
+// commits are multicast to both CTAs' barriers.  Per CTA this halves the B
+// bytes moved from L2 for the same MMA work.
 //
 // The kernel is persistent (grid <= #SMs, static round-robin over work units)
 // and double-buffers the TMEM accumulator (2 x BN columns), so the epilogue of
@@ -30,7 +38,7 @@
 
 namespace idb {
 
-constexpr int kBM = 128;          // rows per CTA tile: one M=128 tcgen05.mma
+constexpr int kBM = 128;          // rows per CTA: one TMEM lane per row
 constexpr int kBK = 64;           // K per pipeline stage: one 128-byte fp16 swizzle row
 constexpr int kUmmaK = 16;        // K per tcgen05.mma.kind::f16
 constexpr int kEpiWarps = 4;      // one warpgroup covers the 128 TMEM lanes
@@ -41,9 +49,9 @@ constexpr int kCounterSlots = 65536;  // split-K tile tickets at the head of the
 
 struct GemmParams {
   int M, N, K;
-  int tiles_m, tiles_n;
+  int tiles_m, tiles_n;   // tiles of (128 * CG) x BN
   int num_tiles;
-  int split_k;    // >= 1, <= kb_total
+  int split_k;    // >= 1, <= kb_total (1 when CG = 2)
   int kb_total;   // ceil(K / kBK)
   int raster;     // 0: groups of `group` tile-rows, M fastest; 1: groups of tile-columns, N fastest
   int group;      // >= 1
@@ -55,10 +63,11 @@ struct GemmParams {
   int* err;                 // device error word
 };
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int CG>
 struct SmemPlan {
+  static constexpr int kBNc = BN / CG;                          // B columns held by this CTA
   static constexpr int kABytes = kBM * kBK * 2;                 // 16 KiB
-  static constexpr int kBBytes = kBK * BN * 2;                  // BN x 128 B
+  static constexpr int kBBytes = kBK * kBNc * 2;                // kBNc x 128 B
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kCBufBytes = kStoreRows * kStoreCols * 2;  // 4 KiB
   static constexpr int kCBytes = kEpiWarps * 2 * kCBufBytes;      // double-buffered per warp
@@ -75,7 +84,8 @@ struct SmemPlan {
                                         : (2 * BN <= 128) ? 128
                                         : (2 * BN <= 256) ? 256
                                                           : 512;
-  static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be 64..256 in steps of 64");
+  static_assert(CG == 1 || CG == 2, "CTA group of 1 or 2");
+  static_assert(kBNc % 64 == 0 && kBNc >= 64 && BN <= 256, "per-CTA B columns must be 64..256 in steps of 64");
   static_assert(kOffB % 1024 == 0 && kOffC % 1024 == 0, "swizzled buffers need 1024-byte alignment");
 };
 
@@ -122,11 +132,12 @@ __device__ __forceinline__ void stage_row_sw128(uint8_t* buf, int lane, const fl
   }
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int CG>
 __global__ void __launch_bounds__(kNumThreads, 1)
     gemm_f16_sm100(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
-  using Plan = SmemPlan<BN, STAGES>;
+  using Plan = SmemPlan<BN, STAGES, CG>;
+  constexpr int kBNc = Plan::kBNc;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem + Plan::kOffA;
@@ -143,6 +154,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 
   const int warp = static_cast<int>(threadIdx.x >> 5);
   const int lane = static_cast<int>(threadIdx.x & 31);
+  const uint32_t rank = (CG == 2) ? cluster_ctarank() : 0u;   // position in the CTA pair
+  const bool leader = (rank == 0);
+  const int cluster_id = static_cast<int>(blockIdx.x) / CG;
+  const int num_clusters = static_cast<int>(gridDim.x) / CG;
 
   if (threadIdx.x == 0) {
 #pragma unroll
@@ -152,8 +167,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     }
     mbar_init(&tfull_bar[0], 1);
     mbar_init(&tfull_bar[1], 1);
-    mbar_init(&tempty_bar[0], kEpiWarps);
-    mbar_init(&tempty_bar[1], kEpiWarps);
+    // every epilogue warp of every CTA in the group releases the accumulator
+    mbar_init(&tempty_bar[0], kEpiWarps * CG);
+    mbar_init(&tempty_bar[1], kEpiWarps * CG);
     mbar_init(done_bar, 1);
     *abort_flag = 0;
     *last_flag = 0;
@@ -165,11 +181,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     if (p.c_tma) prefetch_tmap(&tmC);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, Plan::kTmemCols);
-    tmem_relinquish();
+    tmem_alloc<CG>(tmem_slot, Plan::kTmemCols);
+    tmem_relinquish<CG>();
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (CG == 2) cluster_sync();   // the peer's barriers are initialised before any remote use
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int num_units = p.num_tiles * p.split_k;
@@ -181,21 +198,35 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+      for (int u = cluster_id; u < num_units && ok; u += num_clusters) {
         int tm, tn, ks, kb0, kb1;
         decode_unit(p, u, tm, tn, ks);
         split_range(p, ks, kb0, kb1);
+        const int arow = tm * (kBM * CG) + static_cast<int>(rank) * kBM;
+        const int bcol = tn * BN + static_cast<int>(rank) * kBNc;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full_bar[stage], Plan::kStageBytes);
-          tma_load_2d(sA + stage * Plan::kABytes, &tmA, &full_bar[stage], kb * kBK, tm * kBM);
+          uint8_t* a_dst = sA + stage * Plan::kABytes;
+          uint8_t* b_dst = sB + stage * Plan::kBBytes;
+          if constexpr (CG == 1) {
+            mbar_arrive_expect_tx(&full_bar[stage], Plan::kStageBytes);
+            tma_load_2d(a_dst, &tmA, &full_bar[stage], kb * kBK, arow);
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j) {
-            tma_load_2d(sB + stage * Plan::kBBytes + j * (kBK * 128), &tmB, &full_bar[stage], tn * BN + j * 64,
-                        kb * kBK);
+            for (int j = 0; j < kBNc / 64; ++j) {
+              tma_load_2d(b_dst + j * (kBK * 128), &tmB, &full_bar[stage], bcol + j * 64, kb * kBK);
+            }
+          } else {
+            // Both CTAs' bytes complete on the even CTA's `full` barrier.
+            if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * Plan::kStageBytes);
+            const uint32_t bar = mapa_shared(smem_u32(&full_bar[stage]), 0);
+            tma_load_2d_pair(a_dst, &tmA, bar, kb * kBK, arow);
+#pragma unroll
+            for (int j = 0; j < kBNc / 64; ++j) {
+              tma_load_2d_pair(b_dst + j * (kBK * 128), &tmB, bar, bcol + j * 64, kb * kBK);
+            }
           }
           ++issued;
           if (++stage == STAGES) {
@@ -210,29 +241,34 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       }
       // Drain: the last min(issued, STAGES) fills must have landed before the
       // CTA may exit (an in-flight TMA write into a retired CTA is undefined).
-      const int outstanding = issued < STAGES ? issued : STAGES;
-      for (int i = 0; i < outstanding; ++i) {
-        stage = (stage == 0) ? STAGES - 1 : stage - 1;
-        if (stage == STAGES - 1) phase ^= 1u;
-        uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(&full_bar[stage], phase)) {
-          if (globaltimer_ns() - t0 > kWaitLimitNs) {
-            atomicOr(p.err, kDevErrTimeoutTeardown);
-            break;
+      // With a CTA pair the fills complete on the even CTA's barriers, which
+      // only that CTA can poll; the odd CTA is covered by the cluster barrier
+      // at teardown, which the even CTA reaches after consuming every fill.
+      if (leader) {
+        const int outstanding = issued < STAGES ? issued : STAGES;
+        for (int i = 0; i < outstanding; ++i) {
+          stage = (stage == 0) ? STAGES - 1 : stage - 1;
+          if (stage == STAGES - 1) phase ^= 1u;
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(&full_bar[stage], phase)) {
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+              atomicOr(p.err, kDevErrTimeoutTeardown);
+              break;
+            }
           }
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16_f32(kBM, BN, /*a_mn_major=*/false, /*b_mn_major=*/true);
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = idesc_f16_f32(kBM * CG, BN, /*a_mn_major=*/false, /*b_mn_major=*/true);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+      for (int u = cluster_id; u < num_units && ok; u += num_clusters) {
         int tm, tn, ks, kb0, kb1;
         decode_unit(p, u, tm, tn, ks);
         split_range(p, ks, kb0, kb1);
@@ -256,16 +292,16 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             const uint64_t ad = smem_desc_sw128(a0 + j * (kUmmaK * 2), 16, 1024);
             // B: N-major, advance 16 K-rows (2 KiB); atoms of 64 columns are kBK*128 B apart.
             const uint64_t bd = smem_desc_sw128(b0 + j * (kUmmaK * 128), kBK * 128, 1024);
-            mma_f16_ss(d_tmem, ad, bd, idesc, (kb > kb0 || j > 0) ? 1u : 0u);
+            mma_f16_ss<CG>(d_tmem, ad, bd, idesc, (kb > kb0 || j > 0) ? 1u : 0u);
           }
-          mma_commit(&empty_bar[stage]);
+          mma_commit<CG>(&empty_bar[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        mma_commit(&tfull_bar[acc]);
+        mma_commit<CG>(&tfull_bar[acc]);
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1u;
@@ -276,7 +312,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         atomicOr(p.err, kDevErrTimeoutMma);
       }
       // Every MMA this thread issued must retire before TMEM is freed.
-      mma_commit(done_bar);
+      mma_commit<CG>(done_bar);
       const uint64_t t0 = globaltimer_ns();
       while (!mbar_try_wait(done_bar, 0)) {
         if (globaltimer_ns() - t0 > kWaitLimitNs) {
@@ -288,14 +324,16 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int ew = warp & 3;               // TMEM lane quarter this warp may access
-    const int row = ew * 32 + lane;        // row inside the 128-row tile
-    const bool leader = (threadIdx.x == 64);
+    const int row = ew * 32 + lane;        // row inside this CTA's 128 rows
+    const bool ticket_thread = (threadIdx.x == 64);
     uint8_t* cbufs = sC + ew * 2 * Plan::kCBufBytes;
+    // the accumulator is released on the even CTA's barrier
+    const uint32_t tempty_remote0 = (CG == 2) ? mapa_shared(smem_u32(&tempty_bar[0]), 0) : 0u;
     int cb = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
+    for (int u = cluster_id; u < num_units; u += num_clusters) {
       int tm, tn, ks;
       decode_unit(p, u, tm, tn, ks);
       // All four warps take the same decision, so none is left waiting at a
@@ -304,12 +342,13 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       if (!ok) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      const int grow = tm * kBM + row;
+      const int cta_row0 = tm * (kBM * CG) + static_cast<int>(rank) * kBM;
+      const int grow = cta_row0 + row;
       const bool row_ok = grow < p.M;
       const int tile = u / p.split_k;
       bool write_c = true;
       float* slots = nullptr;
-      if (p.split_k > 1) {
+      if (CG == 1 && p.split_k > 1) {
         slots = p.partials + static_cast<size_t>(tile) * p.split_k * (kBM * BN);
         float4* mine = reinterpret_cast<float4*>(slots + static_cast<size_t>(ks) * (kBM * BN));
 #pragma unroll 1
@@ -328,7 +367,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
         __threadfence();
         named_bar_sync(1, 32 * kEpiWarps);
-        if (leader) {
+        if (ticket_thread) {
           const unsigned old = atomicAdd(&p.counters[tile], 1u);
           *last_flag = (old == static_cast<unsigned>(p.split_k - 1)) ? 1 : 0;
         }
@@ -348,7 +387,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 #pragma unroll
             for (int i = 0; i < 32; ++i) f[h * 32 + i] = __uint_as_float(v[i]);
           }
-          if (p.split_k > 1) {
+          if (CG == 1 && p.split_k > 1) {
             // Sum the partials in split order (deterministic whichever CTA is last).
             float s[64];
 #pragma unroll
@@ -379,6 +418,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           }
           stage_row_sw128(buf, lane, f);
           const int col0 = tn * BN + c64 * 64;
+          const int row0 = cta_row0 + ew * 32;
           if (p.c_tma) {
             fence_proxy_async_smem();
             __syncwarp();
@@ -386,13 +426,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
               // A box that starts past the edge has nothing to write; skip it
               // but still close a (possibly empty) bulk group so that the
               // wait_group.read<1> accounting above stays per buffer.
-              const int row0 = tm * kBM + ew * 32;
               if (row0 < p.M && col0 < p.N) tma_store_2d(&tmC, buf, col0, row0);
               bulk_commit_group();
             }
           } else {
             __syncwarp();
-            const int row0 = tm * kBM + ew * 32;
             for (int r = 0; r < kStoreRows; ++r) {
               const int gr = row0 + r;
               if (gr >= p.M) break;
@@ -411,11 +449,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           }
           cb ^= 1;
         }
-        if (p.split_k > 1 && leader) p.counters[tile] = 0u;  // leave the ticket zero for the next launch
+        if (CG == 1 && p.split_k > 1 && ticket_thread) p.counters[tile] = 0u;  // ticket zero for the next launch
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      if (lane == 0) {
+        if constexpr (CG == 1) {
+          mbar_arrive(&tempty_bar[acc]);
+        } else {
+          mbar_arrive_cluster(tempty_remote0 + static_cast<uint32_t>(acc * 8));
+        }
+      }
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
@@ -431,9 +475,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   // ------------------------------------------------------------ teardown
   tc_fence_before();
   __syncthreads();
+  // A CTA of a pair may not leave while its peer can still touch its shared
+  // memory (remote arrives, MMA operand reads) or TMEM.
+  if constexpr (CG == 2) cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, Plan::kTmemCols);
+    tmem_dealloc<CG>(tmem_base, Plan::kTmemCols);
   }
 }
 

@@ -1,0 +1,94 @@
+"""Per-shape throughput table: TFLOP/s and % of roofline for every workload shape.
+
+For each shape the dispatched configuration (tuned table entry, else the
+heuristic) is timed with distinct CUDA events, L2 flushed before every
+repetition, on seeded inputs (uniform[-1,1]; skinny shapes A~N(0,1),
+B~N(0,0.02^2)).  The roofline time of a shape is
+max(2MNK / peak_flops, 2(MK+KN+MN) / peak_bw) with fp16 input/output bytes
+only; % of roofline = roofline time / measured time.  Both the nominal B200
+peaks (2250 TFLOP/s dense fp16, 8000 GB/s) and the measured ones
+(MEASURED_PEAKS.json: bf16 GEMM burst, HBM copy) are reported.
+
+    python -m infinite_dreams.bench_shapes [--sets single,square,skinny,irregular]
+                                           [--iters 20] [--out results/shapes.json]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+from pathlib import Path
+from typing import Dict, List, Optional
+
+NOMINAL_TFLOPS = 2250.0
+NOMINAL_GBS = 8000.0
+
+
+def measured_peaks(path: Optional[Path] = None) -> Dict[str, float]:
+    p = path or Path(__file__).resolve().parents[2] / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"tflops": float(d["bf16_tflops"]), "gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"tflops": 1590.0, "gbs": 6650.0, "source": "fallback"}
+
+
+def roofline_ms(M: int, N: int, K: int, tflops: float, gbs: float) -> float:
+    flops = 2.0 * M * N * K
+    nbytes = 2.0 * (M * K + K * N + M * N)
+    return max(flops / (tflops * 1e12), nbytes / (gbs * 1e9)) * 1e3
+
+
+def run(sets: List[str], iters: int, warmup: int, cfg_override: Optional[int] = None) -> List[Dict[str, object]]:
+    import torch
+
+    from . import dispatch, infinite_dreams_ext as ext
+    from .sizes import shape_sets
+    from .tuner import make_bench_cases
+    from .utils import time_cuda_ms
+
+    mp = measured_peaks()
+    rows = []
+    table = ext.gemm_cfg_table_cpu()
+    for name in sets:
+        for (M, N, K) in shape_sets()[name]:
+            (case,) = make_bench_cases([(M, N, K)], seed=0, dist="skinny" if name == "skinny" else "uniform")
+            cid = cfg_override if cfg_override is not None else dispatch.lookup(M, N, K)
+            out = torch.empty((M, N), dtype=torch.float16, device="cuda")
+            ms = time_cuda_ms(lambda: ext.gemm_forward_cfg(case.A, case.B, cid, out=out), iters=iters,
+                              warmup=warmup, flush_l2=True)
+            flops = 2.0 * M * N * K
+            nbytes = 2.0 * (M * K + K * N + M * N)
+            rows.append({
+                "set": name, "M": M, "N": N, "K": K, "cfg_id": cid,
+                "knobs": dict(zip(ext.CFG_COLUMNS, table[cid].tolist())), "ms": ms,
+                "tflops": flops / (ms * 1e-3) / 1e12, "gbs": nbytes / (ms * 1e-3) / 1e9,
+                "pct_fp16_peak_nominal": 100.0 * flops / (ms * 1e-3) / 1e12 / NOMINAL_TFLOPS,
+                "pct_roofline_nominal": 100.0 * roofline_ms(M, N, K, NOMINAL_TFLOPS, NOMINAL_GBS) / ms,
+                "pct_roofline_measured": 100.0 * roofline_ms(M, N, K, mp["tflops"], mp["gbs"]) / ms,
+                "bound": "tensor" if flops / (NOMINAL_TFLOPS * 1e12) > nbytes / (NOMINAL_GBS * 1e9) else "hbm",
+            })
+            del case, out
+            torch.cuda.empty_cache()
+    ext.check_device_errors()
+    return rows
+
+
+def main(argv: Optional[List[str]] = None) -> None:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--sets", default="single,square,skinny,irregular")
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--cfg", type=int, default=None)
+    ap.add_argument("--out", default="results/shapes.json")
+    args = ap.parse_args(argv)
+    rows = run(args.sets.split(","), args.iters, args.warmup, args.cfg)
+    os.makedirs(os.path.dirname(args.out) or ".", exist_ok=True)
+    Path(args.out).write_text(json.dumps(rows, indent=1) + "\n")
+    for r in rows:
+        print(f"{r['set']:9s} {r['M']:6d} {r['N']:6d} {r['K']:6d}  {r['ms']:8.4f} ms  {r['tflops']:7.1f} TF/s "
+              f"{r['gbs']:7.0f} GB/s  {r['pct_roofline_nominal']:5.1f}% roof(nom) "
+              f"{r['pct_roofline_measured']:5.1f}% roof(meas)  {r['bound']}  {tuple(r['knobs'].values())}")
+
+
+if __name__ == "__main__":
+    main()

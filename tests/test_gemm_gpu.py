@@ -19,9 +19,9 @@ def _ext():
     return infinite_dreams_ext
 
 
-def _cfg(tile_n=128, stages=4, raster=0, group=8, split_k=1):
+def _cfg(tile_n=128, stages=4, raster=0, group=8, split_k=1, mma_sm=1):
     from infinite_dreams import _capi
-    cid = _capi.cfg_find((128, tile_n, 64, stages, 1, raster, group, split_k))
+    cid = _capi.cfg_find((128 * mma_sm, tile_n, 64, stages, mma_sm, raster, group, split_k))
     assert cid >= 0
     return cid
 
@@ -50,6 +50,23 @@ def test_one_tile_exact_shape(cuda_device):
 def test_every_instantiation(cuda_device, tile_n, stages):
     """Each compiled (tile_n, stages) kernel on a shape with ragged M/N/K edges."""
     _check(320, 704, 328, _cfg(tile_n, stages), seed=tile_n + stages)
+
+
+@pytest.mark.parametrize("tile_n,stages", [(128, 2), (128, 5), (128, 8), (256, 2), (256, 4), (256, 6)])
+def test_every_pair_instantiation(cuda_device, tile_n, stages):
+    """CTA-pair (tcgen05 cta_group::2, 256-row tiles) kernels on ragged edges."""
+    _check(320, 704, 328, _cfg(tile_n, stages, mma_sm=2), seed=100 + tile_n + stages)
+
+
+@pytest.mark.parametrize("M", [100, 130, 256, 383, 520])
+def test_pair_partial_row_tiles(cuda_device, M):
+    """M=100: the odd CTA of the pair has no valid rows; M=130: two of them."""
+    _check(M, 512, 192, _cfg(256, 4, mma_sm=2), seed=M)
+
+
+@pytest.mark.parametrize("raster,group", [(0, 1), (0, 4), (1, 2), (1, 16)])
+def test_pair_raster_orders(cuda_device, raster, group):
+    _check(1100, 1536, 256, _cfg(256, 6, raster, group, mma_sm=2), seed=raster * 7 + group)
 
 
 @pytest.mark.parametrize("raster,group", [(0, 1), (0, 16), (1, 1), (1, 4)])

@@ -33,11 +33,20 @@ def test_every_valid_combination_is_in_the_menu():
 
 def test_smem_fits_and_max_stages_per_tile():
     menu = gen.enumerate_menu()
-    for bn, st in gen.variants(menu):
-        assert gen.smem_bytes(128, bn, 64, st) <= gen.SMEM_CAP
+    for bn, st, sm in gen.variants(menu):
+        assert gen.smem_bytes(128 * sm, bn, 64, st, sm) <= gen.SMEM_CAP
         assert gen.tmem_cols(bn) <= 512
-    deepest = {bn: max(st for b, st in gen.variants(menu) if b == bn) for bn in gen.TILE_NS}
-    assert deepest == {64: 8, 128: 6, 192: 4, 256: 4}
+    deepest = {(bn, sm): max(st for b, st, s in gen.variants(menu) if (b, s) == (bn, sm))
+               for bn, _, sm in gen.variants(menu)}
+    assert deepest == {(64, 1): 8, (128, 1): 6, (192, 1): 4, (256, 1): 4, (128, 2): 8, (256, 2): 6}
+
+
+def test_pair_rules():
+    assert gen.valid((256, 256, 64, 6, 2, 0, 8, 1))
+    assert not gen.valid((256, 256, 64, 6, 2, 0, 8, 2))   # no split-K for CTA pairs
+    assert not gen.valid((256, 192, 64, 4, 2, 0, 8, 1))   # 96 columns per CTA is not a 64-column atom
+    assert not gen.valid((256, 64, 64, 4, 2, 0, 8, 1))
+    assert not gen.valid((256, 256, 64, 7, 2, 0, 8, 1))   # shared memory
 
 
 def test_generated_files_up_to_date():
