@@ -362,10 +362,13 @@ def run_ours(args: argparse.Namespace) -> None:
         return
 
     pk = peaks()
-    peak = float(pk["bf16_tflops"])
+    # The timed region is ~0.5-1 s of back-to-back GEMMs, which runs under the
+    # power cap: the sustained GEMM figure is the matching denominator.
+    peak = float(pk["bf16_tflops_sustained"])
     achieved = 2.0 * M * N * K / (kern_ms * 1e-3) / 1e12
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak, "peak_source": f"{pk['source']} bf16 dense burst",
+                "frac": achieved / peak, "peak_source": f"{pk['source']} bf16 dense GEMM, sustained",
+                "frac_of_burst": achieved / float(pk["bf16_tflops"]),
                 "frac_of_nominal_2250": achieved / NOMINAL_FP16_TFLOPS,
                 "kernel": f"gemm_f16_sm100<{knobs['tile_n']},{knobs['stages']}>",
                 "algorithmic_flop_per_launch": 2.0 * M * N * K, "launch_ms": kern_ms,
