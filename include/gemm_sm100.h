@@ -104,6 +104,27 @@ int gemm_default_cfg(int64_t M, int64_t N, int64_t K);
  * src/gemm_ext.cpp:50). */
 int gemm_device_error(int device, int* code);
 
+/* Size of the static scratch array behind gemm_launch_noalloc (32 MiB). */
+#define GEMM_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
+
+/* gemm_launch for callers that cannot allocate device memory: a runtime that
+ * hands its operators only input/output pointers and a stream, or code that
+ * shares the GPU with a framework whose allocator has reserved nearly all of
+ * its memory (cudaMalloc would fail, fragment that pool, or synchronise the
+ * device).  Same arguments and results as gemm_launch, minus the workspace:
+ * split-K partials, tickets and repacked operands go to a file-scope
+ * __device__ array of GEMM_NOALLOC_SCRATCH_BYTES that every GPU loading the
+ * library keeps until exit.  A problem needing more scratch than that
+ * (gemm_workspace_bytes) returns GEMM_ERR_WORKSPACE without launching.  The
+ * first call on a device looks up the array's address (make it before any
+ * stream capture); each call clears the ticket region on `stream`.  All
+ * calls on a device share the array, so calls whose kernels overlap on the
+ * GPU race; serialise them.  Nothing here calls cudaMalloc or cudaFree.
+ * No counterpart in the reference (its extension allocated C through
+ * torch and used no scratch, src/gemm_ext.cpp:35). */
+int gemm_launch_noalloc(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                        int64_t ldb, int64_t ldc, int cfg_id, void* stream);
+
 /* Message for the calling thread's last failing call ("" if none). */
 const char* gemm_last_error(void);
 

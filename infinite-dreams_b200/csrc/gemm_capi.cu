@@ -334,6 +334,9 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
 }
 
 }  // namespace
+
+void record_last_error(const std::string& msg) { t_last_error = msg; }
+
 }  // namespace idb
 
 using namespace idb;

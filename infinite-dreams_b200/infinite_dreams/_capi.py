@@ -36,6 +36,7 @@ _SIG = [
     ("gemm_launch_knobs", ctypes.c_int,
      [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, ctypes.POINTER(ctypes.c_int), ctypes.c_int, _P,
       ctypes.c_size_t, _P]),
+    ("gemm_launch_noalloc", ctypes.c_int, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, ctypes.c_int, _P]),
     ("gemm_default_cfg", ctypes.c_int, [_I64, _I64, _I64]),
     ("gemm_device_error", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
     ("gemm_last_error", ctypes.c_char_p, []),
