@@ -142,6 +142,9 @@ int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 struct Plan {
   int tile_m = 0, tile_n = 0, stages = 0, cg = 1, raster = 0, group = 1, split_k = 1;
   int tiles_m = 0, tiles_n = 0, num_tiles = 0, kb_total = 0;
+  bool streamk = false;
+  int workers = 0;    // persistent CTAs (CTA pairs for cg = 2)
+  int max_parts = 1;  // partial slots per tile
   bool pack_a = false, pack_b = false;
   size_t off_partials = 0, off_pack_a = 0, off_pack_b = 0, total = 0;
   int64_t lda_packed = 0, ldb_packed = 0;
@@ -149,8 +152,12 @@ struct Plan {
 
 constexpr size_t kCounterBytes = static_cast<size_t>(kCounterSlots) * sizeof(unsigned int);
 
+// Stream-K: the worker that owns (tile, K-block) iteration x when T
+// iterations are split evenly over W workers (same formula as the kernel).
+int64_t sk_owner(int64_t x, int64_t T, int64_t W) { return ((x + 1) * W - 1) / T; }
+
 int make_plan(const void* A, const void* B, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
-              int cfg_id, Plan* pl) {
+              int cfg_id, int sms, Plan* pl) {
   if (cfg_id < 0 || cfg_id >= IDB_MENU_SIZE) {
     return fail(GEMM_ERR_BAD_CFG, "cfg_id " + std::to_string(cfg_id) + " out of range [0, " +
                                       std::to_string(IDB_MENU_SIZE) + ")");
@@ -173,19 +180,37 @@ int make_plan(const void* A, const void* B, int64_t M, int64_t N, int64_t K, int
   pl->num_tiles = static_cast<int>(tiles);
   pl->kb_total = static_cast<int>((K + kBK - 1) / kBK);
   // A split count above the number of K blocks cannot give every slice work;
-  // it is clamped (the result is the same GEMM).
+  // it is clamped (the result is the same GEMM).  split_k = 0 selects
+  // stream-K.
   pl->split_k = row[kColSplitK];
+  pl->streamk = (pl->split_k == 0) && pl->kb_total > 0;
+  if (pl->split_k < 1) pl->split_k = 1;
   if (pl->split_k > pl->kb_total) pl->split_k = pl->kb_total > 0 ? pl->kb_total : 1;
-  if (pl->split_k > 1 && pl->num_tiles > kCounterSlots) {
-    return fail(GEMM_ERR_UNSUPPORTED, "split-K supports at most 65536 output tiles");
+  const int64_t units = static_cast<int64_t>(pl->num_tiles) * pl->split_k;
+  const int64_t slots = sms / pl->cg;
+  pl->workers = static_cast<int>(units < slots ? units : slots);
+  pl->max_parts = pl->split_k;
+  if (pl->streamk) {
+    const int64_t T = static_cast<int64_t>(pl->num_tiles) * pl->kb_total;
+    pl->workers = static_cast<int>(T < slots ? T : slots);
+    int64_t mp = 1;
+    for (int64_t tile = 0; tile < pl->num_tiles; ++tile) {
+      const int64_t t0 = tile * pl->kb_total;
+      const int64_t parts = sk_owner(t0 + pl->kb_total - 1, T, pl->workers) - sk_owner(t0, T, pl->workers) + 1;
+      if (parts > mp) mp = parts;
+    }
+    pl->max_parts = static_cast<int>(mp);
+  }
+  if (pl->max_parts > 1 && pl->num_tiles > kCounterSlots) {
+    return fail(GEMM_ERR_UNSUPPORTED, "split-K / stream-K support at most 65536 output tiles");
   }
   pl->pack_a = M > 0 && K > 0 && !tma_addressable(A, lda);
   pl->pack_b = N > 0 && K > 0 && !tma_addressable(B, ldb);
   size_t off = 0;
-  if (pl->split_k > 1 || pl->pack_a || pl->pack_b) off = kCounterBytes;
-  if (pl->split_k > 1) {
+  if (pl->max_parts > 1 || pl->pack_a || pl->pack_b) off = kCounterBytes;
+  if (pl->max_parts > 1) {
     pl->off_partials = off;
-    off += static_cast<size_t>(pl->num_tiles) * pl->split_k * kBM * pl->tile_n * sizeof(float);
+    off += static_cast<size_t>(pl->num_tiles) * pl->max_parts * kBM * pl->tile_n * sizeof(float);
     off = static_cast<size_t>(round_up(static_cast<int64_t>(off), 256));
   }
   if (pl->pack_a) {
@@ -247,11 +272,15 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
   if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) | reinterpret_cast<uintptr_t>(C)) % 2u) {
     return fail(GEMM_ERR_INVALID_ARG, "A, B and C must be 2-byte aligned (fp16)");
   }
-  Plan pl;
-  int st = make_plan(A, B, M, N, K, lda, ldb, cfg_id, &pl);
-  if (st != GEMM_OK) return st;
+  if (cfg_id < 0 || cfg_id >= IDB_MENU_SIZE) {
+    return fail(GEMM_ERR_BAD_CFG, "cfg_id " + std::to_string(cfg_id) + " out of range [0, " +
+                                      std::to_string(IDB_MENU_SIZE) + ")");
+  }
   DeviceInfo dinfo;
-  st = device_info(&dinfo);
+  int st = device_info(&dinfo);
+  if (st != GEMM_OK) return st;
+  Plan pl;
+  st = make_plan(A, B, M, N, K, lda, ldb, cfg_id, dinfo.sms, &pl);
   if (st != GEMM_OK) return st;
   if (K == 0) {
     // Empty reduction: C = 0 (the reference kernel's loop body never runs).
@@ -315,19 +344,20 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
   p.num_tiles = pl.num_tiles;
   p.split_k = pl.split_k;
   p.kb_total = pl.kb_total;
+  p.streamk = pl.streamk ? 1 : 0;
+  p.max_parts = pl.max_parts;
+  p.total_iters = static_cast<long long>(pl.num_tiles) * pl.kb_total;
   p.raster = pl.raster;
   p.group = pl.group;
   p.c_tma = c_tma ? 1 : 0;
   p.C = static_cast<__half*>(C);
   p.ldc = ldc;
-  p.partials = pl.split_k > 1 ? reinterpret_cast<float*>(wsb + pl.off_partials) : nullptr;
-  p.counters = pl.split_k > 1 ? reinterpret_cast<unsigned int*>(wsb) : nullptr;
+  p.partials = pl.max_parts > 1 ? reinterpret_cast<float*>(wsb + pl.off_partials) : nullptr;
+  p.counters = pl.max_parts > 1 ? reinterpret_cast<unsigned int*>(wsb) : nullptr;
   p.err = err_word;
 
-  const int64_t units = static_cast<int64_t>(pl.num_tiles) * pl.split_k;
   // persistent grid: one CTA (or CTA pair) per SM (pair), at most one per work unit
-  const int64_t slots = dinfo.sms / pl.cg;
-  const int grid = static_cast<int>((units < slots ? units : slots) * pl.cg);
+  const int grid = pl.workers * pl.cg;
   e = var->fn(tmA, tmB, tmC, p, grid, stream);
   if (e != cudaSuccess) return fail_cuda(e, "gemm kernel launch");
   return GEMM_OK;
@@ -380,7 +410,16 @@ size_t gemm_workspace_bytes(const void* A, const void* B, int64_t M, int64_t N, 
                             int64_t ldb, int cfg_id) {
   Plan pl;
   if (M <= 0 || N <= 0 || K <= 0) return 0;
-  if (make_plan(A, B, M, N, K, lda, ldb, cfg_id, &pl) != GEMM_OK) return 0;
+  // Stream-K workspace depends on the SM count of the current device (148
+  // on a B200; assumed when no device is visible).
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0) sms = v;
+  } else {
+    cudaGetLastError();
+  }
+  if (make_plan(A, B, M, N, K, lda, ldb, cfg_id, sms, &pl) != GEMM_OK) return 0;
   return pl.total;
 }
 

@@ -15,9 +15,9 @@
 //   warps 2..5  epilogue: tcgen05.ld (32 lanes x 32 columns per warp), fp16
 //               conversion, 128B-swizzled smem staging, TMA store (or a
 //               coalesced st.global path when C's row pitch is not 16-byte
-//               aligned).  Split-K partials go to an fp32 workspace; the last
-//               CTA of a tile (atomic ticket, no spinning) sums the partials
-//               in split order and writes C.
+//               aligned).  Split-K / stream-K partials go to an fp32
+//               workspace; the last CTA of a tile (atomic ticket, no
+//               spinning) sums the partials in K order and writes C.
 //
 // CG (CTA group) = 1: one CTA owns a 128 x BN tile (MMA M=128).
 // CG = 2: a cluster of two CTAs owns a 256 x BN tile (tcgen05 cta_group::2,
@@ -51,14 +51,17 @@ struct GemmParams {
   int M, N, K;
   int tiles_m, tiles_n;   // tiles of (128 * CG) x BN
   int num_tiles;
-  int split_k;    // >= 1, <= kb_total (1 when CG = 2)
+  int split_k;    // >= 1, <= kb_total (1 when CG = 2); 1 in stream-K mode
   int kb_total;   // ceil(K / kBK)
+  int streamk;    // 1: stream-K (CG = 1 only), each worker owns an equal share of all (tile, K-block) iterations
+  int max_parts;  // partial slots per tile in the workspace (split_k, or the most stream-K pieces of any tile)
+  long long total_iters;  // num_tiles * kb_total
   int raster;     // 0: groups of `group` tile-rows, M fastest; 1: groups of tile-columns, N fastest
   int group;      // >= 1
   int c_tma;      // 1: TMA-store epilogue; 0: coalesced st.global epilogue (any pitch)
   __half* C;
   long long ldc;
-  float* partials;          // split-K fp32 partial tiles (tile, split, 128 x BN)
+  float* partials;          // fp32 partial tiles (tile, part, 128 x BN) of split-K / stream-K
   unsigned int* counters;   // split-K tickets, zero on entry and on exit
   int* err;                 // device error word
 };
@@ -89,10 +92,8 @@ struct SmemPlan {
   static_assert(kOffB % 1024 == 0 && kOffC % 1024 == 0, "swizzled buffers need 1024-byte alignment");
 };
 
-// Work unit -> (tile row, tile column, split index).
-__device__ __forceinline__ void decode_unit(const GemmParams& p, int u, int& tm, int& tn, int& ks) {
-  ks = u % p.split_k;
-  const int t = u / p.split_k;
+// Tile index -> (tile row, tile column) in grouped raster order.
+__device__ __forceinline__ void tile_coords(const GemmParams& p, int t, int& tm, int& tn) {
   if (p.raster == 0) {
     const int per_group = p.group * p.tiles_n;
     const int g = t / per_group;
@@ -112,9 +113,138 @@ __device__ __forceinline__ void decode_unit(const GemmParams& p, int u, int& tm,
   }
 }
 
-__device__ __forceinline__ void split_range(const GemmParams& p, int ks, int& kb0, int& kb1) {
-  kb0 = static_cast<int>((static_cast<long long>(ks) * p.kb_total) / p.split_k);
-  kb1 = static_cast<int>((static_cast<long long>(ks + 1) * p.kb_total) / p.split_k);
+// One piece of work: tile (tm, tn), K blocks [kb0, kb1), and which of the
+// tile's `nparts` K pieces it is (nparts = 1: the whole K range, written
+// straight to C; otherwise a partial tile reduced by the last arriving CTA).
+struct Unit {
+  int tile, tm, tn, kb0, kb1, part, nparts;
+  bool down;  // walk K from the end
+};
+
+// This worker's position in its list of units.
+//  * data-parallel / split-K: units u = worker, worker + workers, ...;
+//    u -> (tile u / split_k, K slice u % split_k).  The persistent workers
+//    advance through their units in lock-step waves, and every other wave
+//    walks K from the end (serpentine order): consecutive waves share operand
+//    blocks, and the K slices a wave touched last are the ones still in L2.
+//  * stream-K: the worker owns iterations [worker*T/W, (worker+1)*T/W) of the
+//    T = num_tiles * kb_total (tile, K-block) iterations, cut at tile
+//    boundaries, so every SM gets the same amount of MMA work whatever the
+//    tile count.
+struct WorkIter {
+  long long cur, end;
+  int count;
+};
+
+__device__ __forceinline__ WorkIter work_begin(const GemmParams& p, int worker, int workers) {
+  WorkIter w;
+  if (p.streamk) {
+    w.cur = static_cast<long long>(worker) * p.total_iters / workers;
+    w.end = static_cast<long long>(worker + 1) * p.total_iters / workers;
+  } else {
+    w.cur = worker;
+    w.end = static_cast<long long>(p.num_tiles) * p.split_k;
+  }
+  w.count = 0;
+  return w;
+}
+
+// Worker that owns stream-K iteration x.
+__device__ __forceinline__ int sk_owner(const GemmParams& p, long long x, int workers) {
+  return static_cast<int>(((x + 1) * workers - 1) / p.total_iters);
+}
+
+__device__ __forceinline__ bool work_next(const GemmParams& p, int worker, int workers, WorkIter& it, Unit& w) {
+  if (it.cur >= it.end) return false;
+  const int kbt = p.kb_total;
+  if (p.streamk) {
+    w.tile = static_cast<int>(it.cur / kbt);
+    w.kb0 = static_cast<int>(it.cur - static_cast<long long>(w.tile) * kbt);
+    const long long left = it.end - it.cur;
+    w.kb1 = (left < kbt - w.kb0) ? w.kb0 + static_cast<int>(left) : kbt;
+    it.cur += w.kb1 - w.kb0;
+    const long long t0 = static_cast<long long>(w.tile) * kbt;
+    const int first = sk_owner(p, t0, workers);
+    w.part = worker - first;
+    w.nparts = sk_owner(p, t0 + kbt - 1, workers) - first + 1;
+    w.down = false;
+  } else {
+    const int u = static_cast<int>(it.cur);
+    w.tile = u / p.split_k;
+    w.part = u - w.tile * p.split_k;
+    w.nparts = p.split_k;
+    w.kb0 = static_cast<int>((static_cast<long long>(w.part) * kbt) / p.split_k);
+    w.kb1 = static_cast<int>((static_cast<long long>(w.part + 1) * kbt) / p.split_k);
+    w.down = (it.count & 1) != 0;
+    it.cur += workers;
+  }
+  tile_coords(p, w.tile, w.tm, w.tn);
+  ++it.count;
+  return true;
+}
+
+// Reduction of a split tile by the 128 epilogue threads of the CTA that
+// brought its last K piece: C[row0 + r][col0 + c] = sum over parts (in K
+// order) of the fp32 partial slots, for the tile's valid rows/columns.  The
+// work is spread over (row, 4-column group) pairs, rows fastest so that
+// partial reads coalesce, with the loads of two parts x 8 elements in flight
+// per thread.  The sum order is fixed, so the result does not depend on which
+// CTA finishes last.
+template <int BN>
+__device__ __forceinline__ void reduce_partials(const GemmParams& p, const float* slots, int nparts, int row0,
+                                                int col0, int et) {
+  const int R = min(kBM, p.M - row0);
+  const int cols = min(BN, p.N - col0);
+  const int C4 = (cols + 3) >> 2;
+  const int E = R * C4;
+  const bool vec = (((reinterpret_cast<uintptr_t>(p.C) | static_cast<uintptr_t>(p.ldc * 2)) & 7u) == 0);
+  constexpr int kB = 8;
+  for (int e0 = et; e0 < E; e0 += kEpiWarps * 32 * kB) {
+    float4 acc[kB];
+#pragma unroll
+    for (int b = 0; b < kB; ++b) acc[b] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = 0; s < nparts; s += 2) {
+      const float4* sa = reinterpret_cast<const float4*>(slots + static_cast<size_t>(s) * (kBM * BN));
+      const float4* sb = reinterpret_cast<const float4*>(slots + static_cast<size_t>(s + 1) * (kBM * BN));
+      const bool two = (s + 1 < nparts);
+      float4 xa[kB], xb[kB];
+#pragma unroll
+      for (int b = 0; b < kB; ++b) {
+        const int e = e0 + b * kEpiWarps * 32;
+        xa[b] = make_float4(0.f, 0.f, 0.f, 0.f);
+        xb[b] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (e < E) {
+          const int r = e % R, j4 = e / R;
+          xa[b] = __ldcg(&sa[j4 * kBM + r]);
+          if (two) xb[b] = __ldcg(&sb[j4 * kBM + r]);
+        }
+      }
+#pragma unroll
+      for (int b = 0; b < kB; ++b) {
+        acc[b].x += xa[b].x; acc[b].y += xa[b].y; acc[b].z += xa[b].z; acc[b].w += xa[b].w;
+        if (two) {
+          acc[b].x += xb[b].x; acc[b].y += xb[b].y; acc[b].z += xb[b].z; acc[b].w += xb[b].w;
+        }
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < kB; ++b) {
+      const int e = e0 + b * kEpiWarps * 32;
+      if (e >= E) continue;
+      const int r = e % R, j4 = e / R;
+      const int gc = col0 + 4 * j4;
+      __half* dst = p.C + static_cast<long long>(row0 + r) * p.ldc + gc;
+      if (vec && gc + 3 < p.N) {
+        uint2 hv;
+        hv.x = pack_half2(acc[b].x, acc[b].y);
+        hv.y = pack_half2(acc[b].z, acc[b].w);
+        *reinterpret_cast<uint2*>(dst) = hv;
+      } else {
+        const float vals[4] = {acc[b].x, acc[b].y, acc[b].z, acc[b].w};
+        for (int c = 0; c < 4 && gc + c < p.N; ++c) dst[c] = __float2half_rn(vals[c]);
+      }
+    }
+  }
 }
 
 // Converts 64 fp32 values of one row to fp16 and writes them as row `lane`
@@ -189,7 +319,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   if constexpr (CG == 2) cluster_sync();   // the peer's barriers are initialised before any remote use
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int num_units = p.num_tiles * p.split_k;
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -198,14 +327,15 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      for (int u = cluster_id; u < num_units && ok; u += num_clusters) {
-        int tm, tn, ks, kb0, kb1;
-        decode_unit(p, u, tm, tn, ks);
-        split_range(p, ks, kb0, kb1);
-        const int arow = tm * (kBM * CG) + static_cast<int>(rank) * kBM;
-        const int bcol = tn * BN + static_cast<int>(rank) * kBNc;
-        for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) {
+      WorkIter wi = work_begin(p, cluster_id, num_clusters);
+      Unit w;
+      while (ok && work_next(p, cluster_id, num_clusters, wi, w)) {
+        const int arow = w.tm * (kBM * CG) + static_cast<int>(rank) * kBM;
+        const int bcol = w.tn * BN + static_cast<int>(rank) * kBNc;
+        for (int it = w.kb0; it < w.kb1; ++it) {
+          const int kb = w.down ? w.kb1 - 1 - (it - w.kb0) : it;
+          // the first STAGES fills go to slots that have never been used
+          if (issued >= STAGES && !mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) {
             ok = false;
             break;
           }
@@ -268,16 +398,20 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int u = cluster_id; u < num_units && ok; u += num_clusters) {
-        int tm, tn, ks, kb0, kb1;
-        decode_unit(p, u, tm, tn, ks);
-        split_range(p, ks, kb0, kb1);
-        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag)) {
+      WorkIter wi = work_begin(p, cluster_id, num_clusters);
+      Unit w;
+      while (ok && work_next(p, cluster_id, num_clusters, wi, w)) {
+        const int kb0 = w.kb0, kb1 = w.kb1;
+        // the first two units use accumulators that have never been used
+        if (wi.count > 2 && !mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        // (the K order of this unit only matters to the producer; the MMA
+        //  consumes stages in arrival order and starts a fresh accumulator
+        //  on the unit's first stage)
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, abort_flag)) {
             ok = false;
@@ -333,9 +467,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     bool ok = true;
-    for (int u = cluster_id; u < num_units; u += num_clusters) {
-      int tm, tn, ks;
-      decode_unit(p, u, tm, tn, ks);
+    WorkIter wi = work_begin(p, cluster_id, num_clusters);
+    Unit w;
+    while (work_next(p, cluster_id, num_clusters, wi, w)) {
+      const int tm = w.tm, tn = w.tn;
       // All four warps take the same decision, so none is left waiting at a
       // later named barrier if another gave up.
       ok = named_bar_and(1, 32 * kEpiWarps, mbar_wait(&tfull_bar[acc], acc_phase, abort_flag));
@@ -345,12 +480,13 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       const int cta_row0 = tm * (kBM * CG) + static_cast<int>(rank) * kBM;
       const int grow = cta_row0 + row;
       const bool row_ok = grow < p.M;
-      const int tile = u / p.split_k;
-      bool write_c = true;
+      const int tile = w.tile;
+      const bool partial = (CG == 1) && (w.nparts > 1);
       float* slots = nullptr;
-      if (CG == 1 && p.split_k > 1) {
-        slots = p.partials + static_cast<size_t>(tile) * p.split_k * (kBM * BN);
-        float4* mine = reinterpret_cast<float4*>(slots + static_cast<size_t>(ks) * (kBM * BN));
+      if (partial) {
+        // 1. this CTA's K piece of the tile -> its partial slot (valid rows only)
+        slots = p.partials + static_cast<size_t>(tile) * p.max_parts * (kBM * BN);
+        float4* mine = reinterpret_cast<float4*>(slots + static_cast<size_t>(w.part) * (kBM * BN));
 #pragma unroll 1
         for (int c32 = 0; c32 < BN / 32; ++c32) {
           uint32_t v[32];
@@ -365,17 +501,37 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             }
           }
         }
+        // 2. ticket: the CTA that brings the tile's last piece reduces it
         __threadfence();
         named_bar_sync(1, 32 * kEpiWarps);
         if (ticket_thread) {
           const unsigned old = atomicAdd(&p.counters[tile], 1u);
-          *last_flag = (old == static_cast<unsigned>(p.split_k - 1)) ? 1 : 0;
+          *last_flag = (old == static_cast<unsigned>(w.nparts - 1)) ? 1 : 0;
         }
         named_bar_sync(1, 32 * kEpiWarps);
-        write_c = (*last_flag != 0);
-        if (write_c) __threadfence();
+        const bool last = (*last_flag != 0);
+        // Few valid rows (skinny M): all 128 threads reduce from the slots and
+        // the accumulator is released at once.  Many rows: the per-row path
+        // below keeps this CTA's piece in TMEM and stores through TMA.
+        const bool coop = (p.M - cta_row0) <= 32;
+        if (!last || coop) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+          if (last) {
+            __threadfence();
+            reduce_partials<BN>(p, slots, w.nparts, cta_row0, tn * BN, static_cast<int>(threadIdx.x) - 64);
+            if (ticket_thread) p.counters[tile] = 0u;  // ticket zero for the next launch
+          }
+          if (++acc == 2) {
+            acc = 0;
+            acc_phase ^= 1u;
+          }
+          continue;
+        }
+        __threadfence();
       }
-      if (write_c) {
+      {
 #pragma unroll 1
         for (int c64 = 0; c64 < BN / 64; ++c64) {
           float f[64];
@@ -387,24 +543,27 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 #pragma unroll
             for (int i = 0; i < 32; ++i) f[h * 32 + i] = __uint_as_float(v[i]);
           }
-          if (CG == 1 && p.split_k > 1) {
-            // Sum the partials in split order (deterministic whichever CTA is last).
+          if (partial) {
+            // Sum the pieces in K order (deterministic whichever CTA is last);
+            // this CTA's own piece comes from TMEM.
             float s[64];
 #pragma unroll
             for (int i = 0; i < 64; ++i) s[i] = 0.0f;
-            for (int s2 = 0; s2 < p.split_k; ++s2) {
-              if (s2 == ks) {
+            for (int s2 = 0; s2 < w.nparts; ++s2) {
+              if (s2 == w.part) {
 #pragma unroll
                 for (int i = 0; i < 64; ++i) s[i] += f[i];
               } else if (row_ok) {
                 const float4* src = reinterpret_cast<const float4*>(slots + static_cast<size_t>(s2) * (kBM * BN));
+                float4 x[16];
+#pragma unroll
+                for (int q = 0; q < 16; ++q) x[q] = __ldcg(&src[(c64 * 16 + q) * kBM + row]);
 #pragma unroll
                 for (int q = 0; q < 16; ++q) {
-                  const float4 x = __ldcg(&src[(c64 * 16 + q) * kBM + row]);
-                  s[4 * q] += x.x;
-                  s[4 * q + 1] += x.y;
-                  s[4 * q + 2] += x.z;
-                  s[4 * q + 3] += x.w;
+                  s[4 * q] += x[q].x;
+                  s[4 * q + 1] += x[q].y;
+                  s[4 * q + 2] += x[q].z;
+                  s[4 * q + 3] += x[q].w;
                 }
               }
             }
@@ -449,7 +608,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           }
           cb ^= 1;
         }
-        if (CG == 1 && p.split_k > 1 && ticket_thread) p.counters[tile] = 0u;  // ticket zero for the next launch
+        if (partial && ticket_thread) p.counters[tile] = 0u;  // ticket zero for the next launch
       }
       tc_fence_before();
       __syncwarp();
@@ -469,7 +628,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       *abort_flag = 1;
       atomicOr(p.err, kDevErrTimeoutEpilogue);
     }
-    if (p.c_tma && lane == 0) bulk_wait_group<0>();
+    // The staging smem must stay valid until the last TMA stores have read it;
+    // their global writes complete with the grid.
+    if (p.c_tma && lane == 0) bulk_wait_group_read<0>();
   }
 
   // ------------------------------------------------------------ teardown

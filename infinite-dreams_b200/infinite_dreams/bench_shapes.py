@@ -38,11 +38,19 @@ def roofline_ms(M: int, N: int, K: int, tflops: float, gbs: float) -> float:
     return max(flops / (tflops * 1e12), nbytes / (gbs * 1e9)) * 1e3
 
 
+def _shapes_of(name: str):
+    """A named shape set, or an explicit shape written MxNxK."""
+    from .sizes import shape_sets
+    if "x" in name:
+        m, n, k = (int(v) for v in name.split("x"))
+        return [(m, n, k)]
+    return shape_sets()[name]
+
+
 def run(sets: List[str], iters: int, warmup: int, cfg_override: Optional[int] = None) -> List[Dict[str, object]]:
     import torch
 
     from . import dispatch, infinite_dreams_ext as ext
-    from .sizes import shape_sets
     from .tuner import make_bench_cases
     from .utils import time_cuda_ms
 
@@ -50,7 +58,7 @@ def run(sets: List[str], iters: int, warmup: int, cfg_override: Optional[int] = 
     rows = []
     table = ext.gemm_cfg_table_cpu()
     for name in sets:
-        for (M, N, K) in shape_sets()[name]:
+        for (M, N, K) in _shapes_of(name):
             (case,) = make_bench_cases([(M, N, K)], seed=0, dist="skinny" if name == "skinny" else "uniform")
             cid = cfg_override if cfg_override is not None else dispatch.lookup(M, N, K)
             out = torch.empty((M, N), dtype=torch.float16, device="cuda")
@@ -75,7 +83,8 @@ def run(sets: List[str], iters: int, warmup: int, cfg_override: Optional[int] = 
 
 def main(argv: Optional[List[str]] = None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("--sets", default="single,square,skinny,irregular")
+    ap.add_argument("--sets", default="single,square,skinny,irregular",
+                    help="comma-separated shape sets (single, square, skinny, irregular, default, large) or MxNxK")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--cfg", type=int, default=None)

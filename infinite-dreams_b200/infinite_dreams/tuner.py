@@ -242,20 +242,39 @@ class TileScorer:
             self._log(key, cfg_id, self.INVALID_MS, 0, 0)
             return self.INVALID_MS
         ms = float(np.mean([self.measure(cfg_id, c, self.opts) for c in self.cases]))
+        if ms >= self.INVALID_MS:
+            self.cache[key] = self.INVALID_MS
+            self._log(key, cfg_id, self.INVALID_MS, 0, 0)
+            return self.INVALID_MS
         self.cache[key] = ms
         self._log(key, cfg_id, ms, 0, 1)
         return ms
 
 
+# Configurations whose workspace would exceed this are scored invalid rather
+# than allocated (split-K partials of a large output grow as tiles x splits).
+MAX_WORKSPACE_BYTES = 1 << 30
+
+
 def _measure_cuda(cfg_id: int, case: BenchCase, opts: ScoreOptions) -> float:
     import torch
 
-    from . import infinite_dreams_ext as ext
+    from . import _capi, infinite_dreams_ext as ext
     from .utils import time_cuda_ms
 
+    need = int(_capi.lib.gemm_workspace_bytes(case.A.data_ptr(), case.B.data_ptr(), case.M, case.N, case.K,
+                                              case.K, case.N, cfg_id))
+    if need > MAX_WORKSPACE_BYTES:
+        return TileScorer.INVALID_MS
     out = torch.empty((case.M, case.N), dtype=torch.float16, device=case.A.device)
-    return time_cuda_ms(lambda: ext.gemm_forward_cfg(case.A, case.B, cfg_id, out=out), iters=opts.iters,
-                        warmup=opts.warmup, flush_l2=opts.flush_l2)
+    try:
+        return time_cuda_ms(lambda: ext.gemm_forward_cfg(case.A, case.B, cfg_id, out=out), iters=opts.iters,
+                            warmup=opts.warmup, flush_l2=opts.flush_l2)
+    except _capi.GemmError as e:
+        # a configuration the shape cannot use (e.g. too many split-K tiles)
+        if e.status in (_capi.GEMM_ERR_UNSUPPORTED, _capi.GEMM_ERR_WORKSPACE):
+            return TileScorer.INVALID_MS
+        raise
 
 
 def differential_evolution_discrete(pop_size: int, generations: int, F: float, CR: float, scorer: TileScorer,
@@ -333,7 +352,8 @@ def rerank_topk(candidates: Sequence[TileConfig], scorer: TileScorer) -> Tuple[L
 def tune(sizes: Sequence[Tuple[int, int, int]], args: argparse.Namespace, menu: Menu,
          dist: str = "uniform") -> Tuple[TileConfig, float, List[Dict[str, Any]]]:
     cases = make_bench_cases(sizes, seed=args.seed, dist=dist)
-    flush = args.flush_l2 or all(2 * (c.M * c.K + c.K * c.N + c.M * c.N) < 96 * 2 ** 20 for c in cases)
+    # Flush L2 between repetitions unless every operand set is well above L2 (126 MB).
+    flush = args.flush_l2 or any(2 * (c.M * c.K + c.K * c.N + c.M * c.N) < 256 * 2 ** 20 for c in cases)
     scorer = TileScorer(cases, ScoreOptions(args.search_iters, args.search_warmup, flush), menu,
                         eval_log_path=args.eval_log)
     best, best_ms, hist = differential_evolution_discrete(args.pop, args.gen, args.F, args.CR, scorer,

@@ -56,6 +56,9 @@ def time_cuda_ms(fn: Callable[[], Any], iters: int, warmup: int, flush_l2: bool 
     total = 0.0
     for _ in range(iters):
         l2_flush()
+        # Keep the GPU busy (untimed) while the host enqueues fn(), so the
+        # interval between the events holds only device work.
+        torch.cuda._sleep(400000)
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)
         start.record()

@@ -71,6 +71,26 @@ def test_workspace_sizing():
     assert ws == cnt + 64 * 64 * 2
 
 
+def _streamk_parts(num_tiles, kbt, workers):
+    T = num_tiles * kbt
+    owner = lambda x: ((x + 1) * workers - 1) // T
+    return max(owner(t * kbt + kbt - 1) - owner(t * kbt) + 1 for t in range(num_tiles))
+
+
+def test_streamk_workspace_sizing():
+    """split_k = 0: stream-K over 148 workers (the B200 SM count, assumed without a GPU)."""
+    cnt = _capi.lib.gemm_workspace_counter_bytes()
+    aligned = 1 << 20
+    ks = (128, 128, 64, 6, 1, 0, 8, 0)
+    # 32 tiles x 64 K blocks over 148 workers: every tile is shared
+    parts = _streamk_parts(32, 64, 148)
+    assert parts >= 4
+    assert _ws(aligned, aligned, 64, 4096, 4096, 4096, 4096, ks) == cnt + 32 * parts * 128 * 128 * 4
+    # 148 tiles x 8 K blocks: one worker per tile, no partials, no workspace
+    assert _streamk_parts(148, 8, 148) == 1
+    assert _ws(aligned, aligned, 128, 148 * 128, 512, 512, 148 * 128, ks) == 0
+
+
 def test_default_cfg_is_in_menu():
     for shape in [(512, 512, 512), (1, 14336, 4096), (16384, 16384, 16384), (7, 12288, 96), (1, 1, 1)]:
         cid = _capi.lib.gemm_default_cfg(*shape)

@@ -79,6 +79,14 @@ def test_split_k(cuda_device, split_k):
     _check(192, 768, 2048, _cfg(128, 4, 0, 8, split_k), seed=split_k)
 
 
+@pytest.mark.parametrize("M,N,K,tile_n", [(64, 4096, 4096, 128), (16, 14336, 4096, 256), (1, 4096, 4096, 64),
+                                           (300, 700, 333, 128), (128, 148 * 128, 512, 128), (1000, 3000, 777, 192),
+                                           (513, 1000, 64, 64)])
+def test_stream_k(cuda_device, M, N, K, tile_n):
+    """split_k = 0: every CTA takes an equal share of all (tile, K-block) iterations."""
+    _check(M, N, K, _cfg(tile_n, 4, 0, 8, 0), dist="skinny", seed=M + N + K)
+
+
 def test_split_k_clamped_to_k_blocks(cuda_device):
     # K=100 has 2 K blocks; split 16 is clamped to 2
     _check(64, 512, 100, _cfg(128, 4, 0, 8, 16))
@@ -113,6 +121,18 @@ def test_pitched_operands(cuda_device):
         assert_close(Cw[:, :N], ref, K, f"pad {pad}")
         if pad:
             assert torch.isnan(Cw[:, N:].float()).all(), "wrote outside the C view"
+
+
+@pytest.mark.parametrize("knobs", [(128, 4, 0, 8, 4), (64, 8, 0, 8, 0)])
+def test_pitched_split_tiles(cuda_device, knobs):
+    """Split-K / stream-K reduction written to a C with an odd pitch (scalar path)."""
+    M, N, K = 70, 300, 520
+    A, B = make_inputs(M, N, K, seed=13)
+    ref = oracle_gemm(A, B)
+    Cw = torch.full((M, N + 3), float("nan"), dtype=torch.float16, device="cuda")
+    capi_gemm(A.cuda(), B.cuda(), _cfg(*knobs), C=Cw, ldc=N + 3, M=M, N=N, K=K)
+    assert_close(Cw[:, :N], ref, K, f"split tiles, pitch {N + 3}")
+    assert torch.isnan(Cw[:, N:].float()).all(), "wrote outside the C view"
 
 
 def test_bad_cfg_raises(cuda_device):

@@ -21,7 +21,9 @@ def test_valid_rules():
     assert not gen.valid((128, 128, 32, 4, 1, 0, 8, 1))   # tile_k is one 128-byte swizzle row
     assert not gen.valid((128, 128, 64, 1, 1, 0, 8, 1))   # at least double buffering
     assert not gen.valid((128, 128, 64, 4, 1, 0, 0, 1))   # group >= 1
-    assert not gen.valid((128, 128, 64, 4, 1, 0, 8, 0))   # split_k >= 1
+    assert gen.valid((128, 128, 64, 4, 1, 0, 8, 0))       # split_k = 0: stream-K
+    assert not gen.valid((128, 128, 64, 4, 1, 0, 8, -1))
+    assert not gen.valid((256, 256, 64, 4, 2, 0, 8, 0))   # no stream-K for CTA pairs
 
 
 def test_every_valid_combination_is_in_the_menu():
