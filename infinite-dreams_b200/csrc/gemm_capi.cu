@@ -446,12 +446,19 @@ int gemm_launch_knobs(const void* A, const void* B, void* C, int64_t M, int64_t 
 
 int gemm_default_cfg(int64_t M, int64_t N, int64_t K) {
   // Heuristic used when no tuned entry exists:
-  //  * enough 256 x 256 tiles to fill the 74 CTA pairs of a B200: CTA-pair
-  //    (cta_group::2) kernel, 4 stages;
+  //  * enough 256 x 512 (else 256 x 256) tiles to fill the 74 CTA pairs of a
+  //    B200: CTA-pair (cta_group::2) kernel, 4 stages;
   //  * otherwise one CTA per 128-row tile, the widest tile_n that still
   //    gives ~one wave, and split-K when the output has too few tiles to
   //    occupy the 148 SMs.
   const int kSms = 148;
+  const int64_t wide_pair_tiles = ((M + 255) / 256) * ((N + 511) / 512);
+  if (wide_pair_tiles >= kSms / 2) {
+    // 256 x 512 tiles on CTA pairs: A is loaded once for two 256-column
+    // halves, the least L2 traffic per FLOP in the bank.
+    int knobs[IDB_MENU_COLS] = {2 * kBM, 512, kBK, 4, 2, 1, 8, 1};
+    return gemm_cfg_find(knobs, IDB_MENU_COLS);
+  }
   const int64_t pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
   if (pair_tiles >= kSms / 2) {
     int knobs[IDB_MENU_COLS] = {2 * kBM, 256, kBK, 4, 2, 0, 8, 1};

@@ -82,13 +82,23 @@ struct SmemPlan {
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kUsed = kOffMisc + 16;
   static constexpr int kDynamicBytes = kUsed + 1024;            // slack for 1024-byte alignment
-  static constexpr uint32_t kTmemCols = (2 * BN <= 32)    ? 32
-                                        : (2 * BN <= 64)  ? 64
-                                        : (2 * BN <= 128) ? 128
-                                        : (2 * BN <= 256) ? 256
-                                                          : 512;
+  // One tcgen05.mma covers at most 256 columns; a 512-column pair tile is two
+  // MMAs per K step, and each CTA holds its half of both MMAs' B columns.
+  static constexpr int kMmaN = BN < 256 ? BN : 256;   // columns per MMA
+  static constexpr int kNumMma = BN / kMmaN;          // MMAs per K step
+  static constexpr int kMmaNc = kMmaN / CG;           // B columns per MMA held by this CTA
+  // Accumulators in TMEM: two (the epilogue of one unit overlaps the next
+  // unit's mainloop) when 2 * BN columns fit in the 512, else one.
+  static constexpr int kNumAcc = (2 * BN <= 512) ? 2 : 1;
+  static constexpr uint32_t kTmemCols = (kNumAcc * BN <= 32)    ? 32
+                                        : (kNumAcc * BN <= 64)  ? 64
+                                        : (kNumAcc * BN <= 128) ? 128
+                                        : (kNumAcc * BN <= 256) ? 256
+                                                                : 512;
   static_assert(CG == 1 || CG == 2, "CTA group of 1 or 2");
-  static_assert(kBNc % 64 == 0 && kBNc >= 64 && BN <= 256, "per-CTA B columns must be 64..256 in steps of 64");
+  static_assert(kBNc % 64 == 0 && kBNc >= 64 && kMmaNc % 64 == 0, "B columns per CTA and MMA: multiples of 64");
+  static_assert(BN <= 256 || (CG == 2 && BN == 512), "a 512-column tile needs a CTA pair");
+  static_assert(kNumAcc * BN <= 512, "TMEM holds 512 fp32 columns");
   static_assert(kOffB % 1024 == 0 && kOffC % 1024 == 0, "swizzled buffers need 1024-byte alignment");
 };
 
@@ -247,6 +257,14 @@ __device__ __forceinline__ void reduce_partials(const GemmParams& p, const float
   }
 }
 
+// Column offset (relative to this CTA's first B column of MMA 0) of the j-th
+// 64-column B atom this CTA holds: atoms are grouped per MMA.
+template <class Plan>
+__device__ __forceinline__ int b_atom_col(int j) {
+  constexpr int kAtomsPerMma = Plan::kMmaNc / 64;
+  return (j / kAtomsPerMma) * Plan::kMmaN + (j % kAtomsPerMma) * 64;
+}
+
 // Converts 64 fp32 values of one row to fp16 and writes them as row `lane`
 // of a [32 x 64] fp16 staging box in the TMA 128-byte swizzle layout.
 __device__ __forceinline__ void stage_row_sw128(uint8_t* buf, int lane, const float (&f)[64]) {
@@ -331,7 +349,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       Unit w;
       while (ok && work_next(p, cluster_id, num_clusters, wi, w)) {
         const int arow = w.tm * (kBM * CG) + static_cast<int>(rank) * kBM;
-        const int bcol = w.tn * BN + static_cast<int>(rank) * kBNc;
+        // this CTA's B columns: its share of every MMA's N range
+        const int bcol = w.tn * BN + static_cast<int>(rank) * Plan::kMmaNc;
         for (int it = w.kb0; it < w.kb1; ++it) {
           const int kb = w.down ? w.kb1 - 1 - (it - w.kb0) : it;
           // the first STAGES fills go to slots that have never been used
@@ -346,7 +365,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             tma_load_2d(a_dst, &tmA, &full_bar[stage], kb * kBK, arow);
 #pragma unroll
             for (int j = 0; j < kBNc / 64; ++j) {
-              tma_load_2d(b_dst + j * (kBK * 128), &tmB, &full_bar[stage], bcol + j * 64, kb * kBK);
+              tma_load_2d(b_dst + j * (kBK * 128), &tmB, &full_bar[stage], bcol + b_atom_col<Plan>(j), kb * kBK);
             }
           } else {
             // Both CTAs' bytes complete on the even CTA's `full` barrier.
@@ -355,7 +374,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             tma_load_2d_pair(a_dst, &tmA, bar, kb * kBK, arow);
 #pragma unroll
             for (int j = 0; j < kBNc / 64; ++j) {
-              tma_load_2d_pair(b_dst + j * (kBK * 128), &tmB, bar, bcol + j * 64, kb * kBK);
+              tma_load_2d_pair(b_dst + j * (kBK * 128), &tmB, bar, bcol + b_atom_col<Plan>(j), kb * kBK);
             }
           }
           ++issued;
@@ -392,7 +411,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && leader) {
-      constexpr uint32_t idesc = idesc_f16_f32(kBM * CG, BN, /*a_mn_major=*/false, /*b_mn_major=*/true);
+      constexpr uint32_t idesc = idesc_f16_f32(kBM * CG, Plan::kMmaN, /*a_mn_major=*/false, /*b_mn_major=*/true);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -402,8 +421,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       Unit w;
       while (ok && work_next(p, cluster_id, num_clusters, wi, w)) {
         const int kb0 = w.kb0, kb1 = w.kb1;
-        // the first two units use accumulators that have never been used
-        if (wi.count > 2 && !mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag)) {
+        // the first kNumAcc units use accumulators that have never been used
+        if (wi.count > Plan::kNumAcc && !mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag)) {
           ok = false;
           break;
         }
@@ -425,8 +444,15 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             // A: K-major, advance 16 elements (32 B) inside the swizzled row.
             const uint64_t ad = smem_desc_sw128(a0 + j * (kUmmaK * 2), 16, 1024);
             // B: N-major, advance 16 K-rows (2 KiB); atoms of 64 columns are kBK*128 B apart.
-            const uint64_t bd = smem_desc_sw128(b0 + j * (kUmmaK * 128), kBK * 128, 1024);
-            mma_f16_ss<CG>(d_tmem, ad, bd, idesc, (kb > kb0 || j > 0) ? 1u : 0u);
+#pragma unroll
+            for (int i = 0; i < Plan::kNumMma; ++i) {
+              // MMA i reads this CTA's atoms [i*kMmaNc/64, (i+1)*kMmaNc/64) and
+              // writes accumulator columns [i*kMmaN, (i+1)*kMmaN).
+              const uint64_t bd = smem_desc_sw128(b0 + i * (Plan::kMmaNc / 64) * (kBK * 128) + j * (kUmmaK * 128),
+                                                  kBK * 128, 1024);
+              mma_f16_ss<CG>(d_tmem + static_cast<uint32_t>(i * Plan::kMmaN), ad, bd, idesc,
+                             (kb > kb0 || j > 0) ? 1u : 0u);
+            }
           }
           mma_commit<CG>(&empty_bar[stage]);
           if (++stage == STAGES) {
@@ -436,7 +462,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
         if (!ok) break;
         mma_commit<CG>(&tfull_bar[acc]);
-        if (++acc == 2) {
+        if (++acc == Plan::kNumAcc) {
           acc = 0;
           acc_phase ^= 1u;
         }
@@ -523,7 +549,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             reduce_partials<BN>(p, slots, w.nparts, cta_row0, tn * BN, static_cast<int>(threadIdx.x) - 64);
             if (ticket_thread) p.counters[tile] = 0u;  // ticket zero for the next launch
           }
-          if (++acc == 2) {
+          if (++acc == Plan::kNumAcc) {
             acc = 0;
             acc_phase ^= 1u;
           }
@@ -619,7 +645,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           mbar_arrive_cluster(tempty_remote0 + static_cast<uint32_t>(acc * 8));
         }
       }
-      if (++acc == 2) {
+      if (++acc == Plan::kNumAcc) {
         acc = 0;
         acc_phase ^= 1u;
       }

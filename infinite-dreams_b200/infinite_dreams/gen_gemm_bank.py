@@ -8,7 +8,8 @@ Blackwell the knobs that matter are different, so the space is redefined:
 
 ===========  ==========================================================
 tile_m       tile rows: 128 * mma_sm (one tcgen05 MMA of M = tile_m)
-tile_n       tile columns: one MMA N <= 256; each CTA holds tile_n / mma_sm
+tile_n       tile columns: one MMA N <= 256, or 512 for a CTA pair (two MMAs
+             per K step, one accumulator); each CTA holds tile_n / mma_sm
              columns of B, a multiple of 64 (one 128-byte swizzle atom)
 tile_k       K per pipeline stage: 64 (one 128-byte swizzle row of fp16)
 stages       depth of the TMA -> shared-memory ring
@@ -47,7 +48,7 @@ TMEM_COLS = 512            # TMEM columns per SM
 BM_PER_SM = 128            # rows one tcgen05 M=128 MMA covers
 
 TILE_MS = (128, 256)
-TILE_NS = (64, 128, 192, 256)
+TILE_NS = (64, 128, 192, 256, 512)
 TILE_KS = (64,)
 STAGES = (2, 3, 4, 5, 6, 7, 8)
 MMA_SMS = (1, 2)
@@ -76,7 +77,8 @@ def smem_bytes(tile_m: int, tile_n: int, tile_k: int, stages: int, mma_sm: int =
 
 
 def tmem_cols(tile_n: int) -> int:
-    need = 2 * tile_n  # double-buffered fp32 accumulator
+    # double-buffered fp32 accumulator when two fit in the 512 columns
+    need = 2 * tile_n if 2 * tile_n <= TMEM_COLS else tile_n
     cols = 32
     while cols < need:
         cols *= 2
@@ -87,7 +89,7 @@ def valid(cfg: Sequence[int]) -> bool:
     tile_m, tile_n, tile_k, stages, mma_sm, raster, group, split_k = cfg
     if mma_sm not in (1, 2) or tile_m != BM_PER_SM * mma_sm:
         return False
-    if tile_n % (64 * mma_sm) != 0 or not (64 <= tile_n <= 256):
+    if tile_n % (64 * mma_sm) != 0 or not (64 <= tile_n <= 256 or (tile_n == 512 and mma_sm == 2)):
         return False
     if tile_k != 64:
         return False

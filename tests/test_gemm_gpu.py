@@ -52,21 +52,24 @@ def test_every_instantiation(cuda_device, tile_n, stages):
     _check(320, 704, 328, _cfg(tile_n, stages), seed=tile_n + stages)
 
 
-@pytest.mark.parametrize("tile_n,stages", [(128, 2), (128, 5), (128, 8), (256, 2), (256, 4), (256, 6)])
+@pytest.mark.parametrize("tile_n,stages", [(128, 2), (128, 5), (128, 8), (256, 2), (256, 4), (256, 6), (512, 2),
+                                           (512, 3), (512, 4)])
 def test_every_pair_instantiation(cuda_device, tile_n, stages):
     """CTA-pair (tcgen05 cta_group::2, 256-row tiles) kernels on ragged edges."""
     _check(320, 704, 328, _cfg(tile_n, stages, mma_sm=2), seed=100 + tile_n + stages)
 
 
 @pytest.mark.parametrize("M", [100, 130, 256, 383, 520])
-def test_pair_partial_row_tiles(cuda_device, M):
+@pytest.mark.parametrize("tile_n", [256, 512])
+def test_pair_partial_row_tiles(cuda_device, M, tile_n):
     """M=100: the odd CTA of the pair has no valid rows; M=130: two of them."""
-    _check(M, 512, 192, _cfg(256, 4, mma_sm=2), seed=M)
+    _check(M, 1000, 192, _cfg(tile_n, 4, mma_sm=2), seed=M)
 
 
 @pytest.mark.parametrize("raster,group", [(0, 1), (0, 4), (1, 2), (1, 16)])
 def test_pair_raster_orders(cuda_device, raster, group):
     _check(1100, 1536, 256, _cfg(256, 6, raster, group, mma_sm=2), seed=raster * 7 + group)
+    _check(1100, 2600, 320, _cfg(512, 4, raster, group, mma_sm=2), seed=raster * 11 + group)
 
 
 @pytest.mark.parametrize("raster,group", [(0, 1), (0, 16), (1, 1), (1, 4)])

@@ -40,7 +40,7 @@ def test_smem_fits_and_max_stages_per_tile():
         assert gen.tmem_cols(bn) <= 512
     deepest = {(bn, sm): max(st for b, st, s in gen.variants(menu) if (b, s) == (bn, sm))
                for bn, _, sm in gen.variants(menu)}
-    assert deepest == {(64, 1): 8, (128, 1): 6, (192, 1): 4, (256, 1): 4, (128, 2): 8, (256, 2): 6}
+    assert deepest == {(64, 1): 8, (128, 1): 6, (192, 1): 4, (256, 1): 4, (128, 2): 8, (256, 2): 6, (512, 2): 4}
 
 
 def test_pair_rules():
@@ -49,6 +49,9 @@ def test_pair_rules():
     assert not gen.valid((256, 192, 64, 4, 2, 0, 8, 1))   # 96 columns per CTA is not a 64-column atom
     assert not gen.valid((256, 64, 64, 4, 2, 0, 8, 1))
     assert not gen.valid((256, 256, 64, 7, 2, 0, 8, 1))   # shared memory
+    assert gen.valid((256, 512, 64, 4, 2, 0, 8, 1))       # 512 columns: two MMAs, one accumulator
+    assert not gen.valid((128, 512, 64, 2, 1, 0, 8, 1))   # 512 columns need a CTA pair
+    assert not gen.valid((256, 512, 64, 5, 2, 0, 8, 1))
 
 
 def test_generated_files_up_to_date():
