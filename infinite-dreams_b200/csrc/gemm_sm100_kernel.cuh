@@ -422,7 +422,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       while (ok && work_next(p, cluster_id, num_clusters, wi, w)) {
         const int kb0 = w.kb0, kb1 = w.kb1;
         // the first kNumAcc units use accumulators that have never been used
-        if (wi.count > Plan::kNumAcc && !mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag)) {
+        // A single accumulator made of two MMA halves (512-column tiles) is
+        // released half by half by the epilogue (tempty_bar[0] / [1]); the
+        // first K block of a unit runs on half 0 before waiting for half 1.
+        constexpr bool kHalves = (Plan::kNumAcc == 1 && Plan::kNumMma == 2);
+        const bool wait_acc = wi.count > Plan::kNumAcc;
+        if (wait_acc && !mbar_wait(&tempty_bar[kHalves ? 0 : acc], acc_phase ^ 1u, abort_flag)) {
           ok = false;
           break;
         }
@@ -439,19 +444,32 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           tc_fence_after();
           const uint32_t a0 = smem_u32(sA + stage * Plan::kABytes);
           const uint32_t b0 = smem_u32(sB + stage * Plan::kBBytes);
-#pragma unroll
-          for (int j = 0; j < kBK / kUmmaK; ++j) {
-            // A: K-major, advance 16 elements (32 B) inside the swizzled row.
+          // MMA i reads this CTA's atoms [i*kMmaNc/64, (i+1)*kMmaNc/64) and
+          // writes accumulator columns [i*kMmaN, (i+1)*kMmaN).  A: K-major,
+          // 16 elements (32 B) per K step inside the swizzled row; B: N-major,
+          // 16 K-rows (2 KiB) per K step, 64-column atoms kBK*128 B apart.
+          auto issue = [&](int i, int j) {
             const uint64_t ad = smem_desc_sw128(a0 + j * (kUmmaK * 2), 16, 1024);
-            // B: N-major, advance 16 K-rows (2 KiB); atoms of 64 columns are kBK*128 B apart.
+            const uint64_t bd = smem_desc_sw128(b0 + i * (Plan::kMmaNc / 64) * (kBK * 128) + j * (kUmmaK * 128),
+                                                kBK * 128, 1024);
+            mma_f16_ss<CG>(d_tmem + static_cast<uint32_t>(i * Plan::kMmaN), ad, bd, idesc,
+                           (kb > kb0 || j > 0) ? 1u : 0u);
+          };
+          if (kHalves && kb == kb0) {
 #pragma unroll
-            for (int i = 0; i < Plan::kNumMma; ++i) {
-              // MMA i reads this CTA's atoms [i*kMmaNc/64, (i+1)*kMmaNc/64) and
-              // writes accumulator columns [i*kMmaN, (i+1)*kMmaN).
-              const uint64_t bd = smem_desc_sw128(b0 + i * (Plan::kMmaNc / 64) * (kBK * 128) + j * (kUmmaK * 128),
-                                                  kBK * 128, 1024);
-              mma_f16_ss<CG>(d_tmem + static_cast<uint32_t>(i * Plan::kMmaN), ad, bd, idesc,
-                             (kb > kb0 || j > 0) ? 1u : 0u);
+            for (int j = 0; j < kBK / kUmmaK; ++j) issue(0, j);
+            if (wait_acc && !mbar_wait(&tempty_bar[1], acc_phase ^ 1u, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int j = 0; j < kBK / kUmmaK; ++j) issue(1, j);
+          } else {
+#pragma unroll
+            for (int j = 0; j < kBK / kUmmaK; ++j) {
+#pragma unroll
+              for (int i = 0; i < Plan::kNumMma; ++i) issue(i, j);
             }
           }
           mma_commit<CG>(&empty_bar[stage]);
@@ -489,6 +507,15 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     uint8_t* cbufs = sC + ew * 2 * Plan::kCBufBytes;
     // the accumulator is released on the even CTA's barrier
     const uint32_t tempty_remote0 = (CG == 2) ? mapa_shared(smem_u32(&tempty_bar[0]), 0) : 0u;
+    // one accumulator in two MMA halves: released half by half (see MMA issuer)
+    constexpr bool kHalvesEpi = (Plan::kNumAcc == 1 && Plan::kNumMma == 2);
+    auto release_acc = [&](int b) {
+      if constexpr (CG == 1) {
+        mbar_arrive(&tempty_bar[b]);
+      } else {
+        mbar_arrive_cluster(tempty_remote0 + static_cast<uint32_t>(b * 8));
+      }
+    };
     int cb = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -633,18 +660,18 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             __syncwarp();
           }
           cb ^= 1;
+          if (kHalvesEpi && c64 == (BN / 64) / 2 - 1) {
+            // first MMA half read out: the next unit's MMAs may start on it
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) release_acc(0);
+          }
         }
         if (partial && ticket_thread) p.counters[tile] = 0u;  // ticket zero for the next launch
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        if constexpr (CG == 1) {
-          mbar_arrive(&tempty_bar[acc]);
-        } else {
-          mbar_arrive_cluster(tempty_remote0 + static_cast<uint32_t>(acc * 8));
-        }
-      }
+      if (lane == 0) release_acc(kHalvesEpi ? 1 : acc);
       if (++acc == Plan::kNumAcc) {
         acc = 0;
         acc_phase ^= 1u;
