@@ -334,13 +334,25 @@ def differential_evolution_discrete(pop_size: int, generations: int, F: float, C
     return final, scorer.score(final), history
 
 
-def rerank_topk(candidates: Sequence[TileConfig], scorer: TileScorer) -> Tuple[List[Tuple[TileConfig, float]],
-                                                                               List[Dict[str, Any]]]:
-    """Re-benchmarks candidates with the scorer's (longer) options; best first."""
+def rerank_topk(candidates: Sequence[TileConfig], scorer: TileScorer, rounds: int = 1
+                ) -> Tuple[List[Tuple[TileConfig, float]], List[Dict[str, Any]]]:
+    """Re-benchmarks candidates with the scorer's (longer) options; best first.
+
+    With rounds > 1 the candidates are measured round-robin, ``rounds`` times
+    each, and ranked by their median.  Interleaving cancels the slow drift of
+    clock and power state on a GPU that runs at its power limit, which a
+    one-after-the-other measurement turns into a ranking bias.
+    """
+    times: Dict[int, List[float]] = {i: [] for i in range(len(candidates))}
+    for r in range(max(1, rounds)):
+        order = range(len(candidates)) if r % 2 == 0 else reversed(range(len(candidates)))
+        for i in order:
+            scorer.set_context("confirm", r, i)
+            scorer.cache.pop(candidates[i].as_tuple(), None)   # measure again every round
+            times[i].append(scorer.score(candidates[i]))
     scored, rows = [], []
     for rank, cfg in enumerate(candidates):
-        scorer.set_context("confirm", -1, rank)
-        ms = scorer.score(cfg)
+        ms = float(np.median(times[rank]))
         scored.append((cfg, ms))
         row = dict(phase="confirm", rank=rank, ms=ms, cfg_id=scorer.menu.cfg_to_id(cfg.as_tuple()))
         row.update(dict(zip(COLUMNS, cfg.as_tuple())))
@@ -362,7 +374,7 @@ def tune(sizes: Sequence[Tuple[int, int, int]], args: argparse.Namespace, menu: 
            if v < TileScorer.INVALID_MS][: args.topk]
     confirm = TileScorer(cases, ScoreOptions(args.confirm_iters, args.confirm_warmup, flush), menu,
                          eval_log_path=args.eval_log)
-    confirmed, rows = rerank_topk(top, confirm)
+    confirmed, rows = rerank_topk(top, confirm, rounds=args.confirm_rounds)
     scorer.close()
     confirm.close()
     hist.extend(rows)
@@ -388,6 +400,7 @@ def main(argv: Optional[Sequence[str]] = None) -> None:
     ap.add_argument("--topk", type=int, default=10)
     ap.add_argument("--confirm-iters", type=int, default=100)
     ap.add_argument("--confirm-warmup", type=int, default=20)
+    ap.add_argument("--confirm-rounds", type=int, default=3, help="interleaved confirmation rounds (median)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--shapes", default="default", help="shape set: " + ", ".join(shape_sets()))
     ap.add_argument("--per-shape", action="store_true", help="tune each shape and persist the dispatch table")

@@ -109,3 +109,31 @@ def test_committed_dispatch_table_is_valid():
         pytest.skip("no committed dispatch table yet")
     for shape, entry in dispatch.entries(dispatch.TABLE_PATH).items():
         assert _capi.cfg_find(entry["knobs"]) >= 0, shape
+
+
+def test_interleaved_confirmation_cancels_drift(menu):
+    """Candidates measured one after the other under a drifting clock rank
+    wrongly; interleaved rounds with a median rank them by their true cost."""
+    true = {(128, 192, 64, 4, 1, 1, 4, 3): 1.00, (128, 256, 64, 4, 1, 0, 8, 1): 1.02}
+    clock = {"t": 0}
+
+    def drifting(cfg_id, case, opts):
+        clock["t"] += 1
+        # the machine slows down by 5% per measurement
+        return true[menu.rows[cfg_id]] * (1.0 + 0.05 * clock["t"])
+
+    case = tuner.BenchCase(M=8, N=8, K=8, A=None, B=None)
+    cands = [tuner.TileConfig(*k) for k in true]
+    s = tuner.TileScorer([case], tuner.ScoreOptions(1, 0), menu, measure=drifting)
+    ranked, _ = tuner.rerank_topk(cands, s, rounds=1)
+    assert ranked[0][0].as_tuple() == (128, 192, 64, 4, 1, 1, 4, 3)   # first measured wins
+    clock["t"] = 0
+    cands_rev = list(reversed(cands))
+    s = tuner.TileScorer([case], tuner.ScoreOptions(1, 0), menu, measure=drifting)
+    ranked, _ = tuner.rerank_topk(cands_rev, s, rounds=1)
+    assert ranked[0][0].as_tuple() == (128, 256, 64, 4, 1, 0, 8, 1)   # order decides: biased
+    clock["t"] = 0
+    s = tuner.TileScorer([case], tuner.ScoreOptions(1, 0), menu, measure=drifting)
+    ranked, rows = tuner.rerank_topk(cands_rev, s, rounds=4)
+    assert ranked[0][0].as_tuple() == (128, 192, 64, 4, 1, 1, 4, 3)   # interleaved: the true best
+    assert len(rows) == 2
