@@ -51,6 +51,9 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
+    ap.add_argument("--ref-shapes", action="store_true",
+                    help="reference arm: also time the reference's CUDA kernel (built from its source) on the GPU "
+                         "for every workload shape")
     return ap.parse_args()
 
 
@@ -204,7 +207,69 @@ def run_reference(args: argparse.Namespace) -> None:
         "note": ("the reference's path is a CUDA kernel with no CPU implementation; this arm times the "
                  "oracle, a C restatement of that kernel's arithmetic (bit-exact to it), on the host cores"),
     }
+    bank = reference_cuda_bank(size, args.ref_shapes)
+    if bank is not None:
+        line["reference_cuda_bank"] = bank
     print(json.dumps(line), flush=True)
+
+
+def reference_cuda_bank(size: int, all_shapes: bool) -> Optional[Dict[str, object]]:
+    """Times the reference's own SIMT kernel (src/gemm_kernels.cuh, compiled
+    from its source into oracle/_ref) on the GPU: the bench workload and, with
+    all_shapes, every workload shape, each with the best of the instantiated
+    tile configurations, back to back like the reference's tuner.
+    Informational; the arm's value is the CPU oracle."""
+    try:
+        import torch
+    except ImportError:  # pragma: no cover
+        return None
+    if not torch.cuda.is_available():
+        return None
+    import oracle
+
+    lib = oracle.load_ref()
+    if lib is None:
+        return None
+    from infinite_dreams.sizes import shape_sets
+
+    cfgs = oracle.ref_cfgs(lib)
+    stream = torch.cuda.current_stream()
+
+    def best(M: int, N: int, K: int, reps: int) -> Optional[Dict[str, object]]:
+        g = torch.Generator(device="cuda")
+        g.manual_seed(0)
+        A = (torch.rand((M, K), generator=g, device="cuda") * 2 - 1).to(torch.float16)
+        B = (torch.rand((K, N), generator=g, device="cuda") * 2 - 1).to(torch.float16)
+        C = torch.empty((M, N), dtype=torch.float16, device="cuda")
+        out = None
+        for cfg in cfgs:
+            def launch(cfg=cfg):
+                return lib.ref_gemm_try(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, *cfg,
+                                        stream.cuda_stream or None)
+            if launch() != 1:
+                continue
+            torch.cuda.synchronize()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for _ in range(reps):
+                launch()
+            e.record()
+            torch.cuda.synchronize()
+            ms = s.elapsed_time(e) / reps
+            if out is None or ms < out["ms"]:
+                out = {"ms": ms, "tflops": 2.0 * M * N * K / (ms * 1e-3) / 1e12, "cfg": list(cfg)}
+        return out
+
+    res = {"kernel": "gemm_tiled_reg (reference SIMT bank, -O3 --use_fast_math, sm_100a)",
+           "workload": dict(best(size, size, size, 1) or {}, shape=[size, size, size])}
+    if all_shapes:
+        res["shapes"] = {}
+        for name, shapes in shape_sets().items():
+            if name == "large":
+                continue
+            for (M, N, K) in shapes:
+                res["shapes"][f"{M}x{N}x{K}"] = best(M, N, K, 3)
+    return res
 
 
 def workload_config(size: int, n: int, knobs: Optional[Dict[str, int]]) -> Dict[str, object]:

@@ -1,0 +1,77 @@
+"""GPU tests of the host layer around the kernels: per-shape dispatch, the DE
+tuner's CUDA scorer, M-row sharding on one device, and the bench contract."""
+import json
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import assert_close, make_inputs, oracle_gemm
+
+pytestmark = pytest.mark.gpu
+ROOT = Path(__file__).resolve().parent.parent
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 512, 512), (16, 14336, 4096), (1000, 3000, 777), (4032, 4128, 3968)])
+def test_dispatch_gemm(cuda_device, M, N, K):
+    """dispatch.gemm picks the tuned configuration and matches the oracle."""
+    from infinite_dreams import dispatch
+    A, B = make_inputs(M, N, K, seed=M + 3)
+    C = dispatch.gemm(A.cuda(), B.cuda())
+    assert_close(C, oracle_gemm(A, B), K, f"dispatch {M}x{N}x{K}")
+
+
+def test_tuner_cuda_scorer_small_search(cuda_device, tmp_path):
+    """A tiny DE search with the real CUDA scorer on one shape; the winner is
+    a menu member, is persisted, and computes the right product."""
+    from infinite_dreams import dispatch, infinite_dreams_ext as ext, tuner
+    from infinite_dreams.gen_gemm_bank import COLUMNS
+    menu = tuner.Menu.from_library()
+    cases = tuner.make_bench_cases([(256, 1024, 512)], seed=1)
+    scorer = tuner.TileScorer(cases, tuner.ScoreOptions(iters=3, warmup=1, flush_l2=True), menu,
+                              eval_log_path=str(tmp_path / "eval.csv"))
+    best, ms, hist = tuner.differential_evolution_discrete(6, 2, 0.7, 0.9, scorer, seed=3, verbose=False)
+    scorer.close()
+    assert menu.cfg_to_id(best.as_tuple()) >= 0 and 0 < ms < 1e3 and len(hist) == 2
+    table = tmp_path / "table.json"
+    dispatch.save_entry(256, 1024, 512, best.as_tuple(), ms, COLUMNS, path=table)
+    cid = dispatch.lookup(256, 1024, 512, table)
+    A, B = cases[0].A, cases[0].B
+    assert_close(ext.gemm_forward_cfg(A, B, cid), oracle_gemm(A.cpu(), B.cpu()), 512, "tuned winner")
+
+
+def test_sharded_single_rank_and_row_blocks(cuda_device):
+    """sharded_gemm on one rank, and row blocks computed separately, equal the whole GEMM."""
+    from infinite_dreams.sharded import row_block, sharded_gemm
+    M, N, K = 1000, 768, 640
+    A, B = make_inputs(M, N, K, seed=21)
+    ref = oracle_gemm(A, B)
+    Ad, Bd = A.cuda(), B.cuda()
+    assert_close(sharded_gemm(Ad, Bd, M_total=M, gather=True), ref, K, "one rank, gathered")
+    parts = []
+    for r in range(3):
+        r0, r1 = row_block(M, 3, r)
+        parts.append(sharded_gemm(Ad[r0:r1].contiguous(), Bd))
+    assert_close(torch.cat(parts, 0), ref, K, "three row blocks")
+
+
+def test_bench_contract_small(cuda_device):
+    """bench.py prints one JSON line with the contract's keys (small size)."""
+    env = dict(os.environ, PYTHONPATH=f"{ROOT / 'infinite-dreams_b200'}:{ROOT}")
+    r = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--size", "2048", "--steps", "4", "--warmup", "3",
+                        "--no-cpu-baseline"], capture_output=True, text=True, env=env, timeout=600, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+                "scaling", "vs_baseline", "dtype", "data", "config", "roofline", "e2e", "gpu_launches", "clocks"):
+        assert key in d, key
+    assert d["n_gpus"] == 1 and d["steps"] == 4 and d["gpu_launches"] == 4
+    assert d["value"] > 50 and np.isfinite(d["roofline"]["frac"])
+    assert d["e2e"]["h2d_bytes_per_step"] == 2 * (2048 * 2048 * 2) and d["e2e"]["d2h_bytes_per_step"] == 2048 * 2048 * 2
+    assert d["config"]["workload"].startswith("gemm 2048x2048x2048")

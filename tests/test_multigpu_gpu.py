@@ -1,0 +1,76 @@
+"""M-row sharding across GPUs with NCCL (skipped with fewer than 2 GPUs).
+
+Each rank computes its contiguous row block of C with the kernel bank; the
+optional all-gather (NCCL) assembles C, which must equal the oracle's."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, M, N, K, q):
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parent.parent
+    for p in (str(root), str(root / "infinite-dreams_b200"), str(root / "tests")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from helpers import make_inputs
+    from infinite_dreams.sharded import broadcast_b, row_block, sharded_gemm
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        A, B = make_inputs(M, N, K, seed=5)
+        Bd = B.to(dev) if rank == 0 else torch.zeros((K, N), dtype=torch.float16, device=dev)
+        broadcast_b(Bd)
+        r0, r1 = row_block(M, world, rank)
+        C = sharded_gemm(A[r0:r1].contiguous().to(dev), Bd, M_total=M, gather=True)
+        torch.cuda.synchronize()
+        q.put((rank, C.cpu().numpy().view(np.uint16)))
+        dist.barrier(device_ids=[rank])
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("M", [2048, 1001])
+def test_sharded_gemm_nccl_allgather(cuda_device, M):
+    world = min(torch.cuda.device_count(), 4)
+    if world < 2:
+        pytest.skip("needs 2 or more GPUs")
+    from helpers import make_inputs, oracle_gemm
+    N, K = 1536, 1024
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, M, N, K, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    A, B = make_inputs(M, N, K, seed=5)
+    ref = oracle_gemm(A, B).astype(np.float32)
+    tol = 1e-2 * np.sqrt(K / 1024) * np.abs(ref).max() + 1e-3
+    for rank, c in results:
+        got = c.view(np.float16).astype(np.float32)
+        assert got.shape == ref.shape
+        assert np.abs(got - ref).max() <= tol, rank
