@@ -247,6 +247,50 @@ int encode_2d(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, 
   return GEMM_OK;
 }
 
+// Recently encoded tensor maps of the calling thread.  A map depends only on
+// the address, extents, pitch and box, so repeated launches on the same
+// buffers (the common case: a tuner loop, a model step) reuse it instead of
+// encoding it again.
+struct MapCacheEntry {
+  const void* base = nullptr;
+  int64_t inner = 0, outer = 0, pitch = 0;
+  int box_inner = 0, box_outer = 0;
+  bool valid = false;
+  CUtensorMap map;
+};
+constexpr int kMapCacheSize = 8;
+thread_local MapCacheEntry t_map_cache[kMapCacheSize];
+thread_local int t_map_next = 0;
+
+int encode_2d_cached(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, int64_t pitch_elems,
+                     int box_inner, int box_outer, const char* what) {
+  for (const MapCacheEntry& e : t_map_cache) {
+    if (e.valid && e.base == base && e.inner == inner && e.outer == outer && e.pitch == pitch_elems &&
+        e.box_inner == box_inner && e.box_outer == box_outer) {
+      *map = e.map;
+      return GEMM_OK;
+    }
+  }
+  const int st = encode_2d(map, base, inner, outer, pitch_elems, box_inner, box_outer, what);
+  if (st != GEMM_OK) return st;
+  MapCacheEntry& e = t_map_cache[t_map_next];
+  t_map_next = (t_map_next + 1) % kMapCacheSize;
+  e.base = base;
+  e.inner = inner;
+  e.outer = outer;
+  e.pitch = pitch_elems;
+  e.box_inner = box_inner;
+  e.box_outer = box_outer;
+  e.map = *map;
+  e.valid = true;
+  return GEMM_OK;
+}
+
+// Device address of the error word, looked up once per device.
+int* g_err_word[kMaxDevices] = {};
+cudaError_t g_err_status[kMaxDevices] = {};
+std::once_flag g_err_once[kMaxDevices];
+
 int launch_pack(const void* src, int64_t lds, void* dst, int64_t ldd, int64_t rows, int64_t cols,
                 cudaStream_t stream) {
   const int64_t chunks = rows * ((cols + 7) / 8);
@@ -321,19 +365,24 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
 
   CUtensorMap tmA, tmB, tmC;
   std::memset(&tmC, 0, sizeof(tmC));
-  st = encode_2d(&tmA, a_src, K, M, a_ld, kBK, kBM, "A");
+  st = encode_2d_cached(&tmA, a_src, K, M, a_ld, kBK, kBM, "A");
   if (st != GEMM_OK) return st;
-  st = encode_2d(&tmB, b_src, N, K, b_ld, 64, kBK, "B");
+  st = encode_2d_cached(&tmB, b_src, N, K, b_ld, 64, kBK, "B");
   if (st != GEMM_OK) return st;
   const bool c_tma = tma_addressable(C, ldc);
   if (c_tma) {
-    st = encode_2d(&tmC, C, N, M, ldc, kStoreCols, kStoreRows, "C");
+    st = encode_2d_cached(&tmC, C, N, M, ldc, kStoreCols, kStoreRows, "C");
     if (st != GEMM_OK) return st;
   }
 
-  int* err_word = nullptr;
-  cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&err_word), g_device_error);
-  if (e != cudaSuccess) return fail_cuda(e, "cudaGetSymbolAddress(g_device_error)");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaGetDevice");
+  std::call_once(g_err_once[dev], [dev] {
+    g_err_status[dev] = cudaGetSymbolAddress(reinterpret_cast<void**>(&g_err_word[dev]), g_device_error);
+  });
+  if (g_err_status[dev] != cudaSuccess) return fail_cuda(g_err_status[dev], "cudaGetSymbolAddress(g_device_error)");
+  int* err_word = g_err_word[dev];
 
   GemmParams p;
   p.M = static_cast<int>(M);
@@ -412,12 +461,13 @@ size_t gemm_workspace_bytes(const void* A, const void* B, int64_t M, int64_t N, 
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   // Stream-K workspace depends on the SM count of the current device (148
   // on a B200; assumed when no device is visible).
-  int sms = 148, dev = 0;
-  if (cudaGetDevice(&dev) == cudaSuccess) {
-    int v = 0;
-    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && v > 0) sms = v;
+  int sms = 148;
+  DeviceInfo dinfo;
+  if (device_info(&dinfo) == GEMM_OK && dinfo.sms > 0) {
+    sms = dinfo.sms;
   } else {
     cudaGetLastError();
+    t_last_error.clear();
   }
   if (make_plan(A, B, M, N, K, lda, ldb, cfg_id, sms, &pl) != GEMM_OK) return 0;
   return pl.total;

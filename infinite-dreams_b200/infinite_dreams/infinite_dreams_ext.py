@@ -80,24 +80,33 @@ def _check_inputs(A: torch.Tensor, B: torch.Tensor) -> None:
 
 
 def _launch(A: torch.Tensor, B: torch.Tensor, cfg_id: int, out: Optional[torch.Tensor]) -> torch.Tensor:
-    M, K = int(A.size(0)), int(A.size(1))
-    N = int(B.size(1))
+    if A.get_device() != torch.cuda.current_device():
+        with torch.cuda.device(A.device):
+            return _launch_here(A, B, cfg_id, out)
+    return _launch_here(A, B, cfg_id, out)
+
+
+def _launch_here(A: torch.Tensor, B: torch.Tensor, cfg_id: int, out: Optional[torch.Tensor]) -> torch.Tensor:
+    """Launch on A's device, which is the current device."""
+    M, K = A.shape
+    N = B.shape[1]
     dev = A.device
-    with torch.cuda.device(dev):
-        A = A.contiguous()
-        B = B.contiguous()
-        if out is None:
-            C = torch.empty((M, N), dtype=torch.float16, device=dev)
-        else:
-            if (out.dtype != torch.float16 or tuple(out.shape) != (M, N) or out.device != dev
-                    or not out.is_contiguous()):
-                raise RuntimeError("out must be a contiguous float16 (M x N) tensor on A's device")
-            C = out
-        stream = torch.cuda.current_stream(dev)
-        need = int(lib.gemm_workspace_bytes(A.data_ptr(), B.data_ptr(), M, N, K, K, N, cfg_id))
-        ws_ptr, ws_len = _workspace(dev, stream, need)
-        st = lib.gemm_launch(A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, K, N, N, cfg_id,
-                             ws_ptr or None, ws_len, stream.cuda_stream or None)
+    A = A.contiguous()
+    B = B.contiguous()
+    if out is None:
+        C = torch.empty((M, N), dtype=torch.float16, device=dev)
+    else:
+        if (out.dtype != torch.float16 or out.shape != (M, N) or out.device != dev
+                or not out.is_contiguous()):
+            raise RuntimeError("out must be a contiguous float16 (M x N) tensor on A's device")
+        C = out
+    stream = torch.cuda.current_stream(dev)
+    a_ptr, b_ptr = A.data_ptr(), B.data_ptr()
+    need = lib.gemm_workspace_bytes(a_ptr, b_ptr, M, N, K, K, N, cfg_id)
+    ws_ptr, ws_len = _workspace(dev, stream, need) if need else (0, 0)
+    st = lib.gemm_launch(a_ptr, b_ptr, C.data_ptr(), M, N, K, K, N, N, cfg_id,
+                         ws_ptr or None, ws_len, stream.cuda_stream or None)
+    if st:
         _capi.check(st, "gemm_launch")
     return C
 
