@@ -502,15 +502,22 @@ int gemm_default_cfg(int64_t M, int64_t N, int64_t K) {
   //    gives ~one wave, and split-K when the output has too few tiles to
   //    occupy the 148 SMs.
   const int kSms = 148;
+  const int64_t pairs = kSms / 2;
+  // Fraction of the last persistent wave's slots that have work.
+  auto wave_fill = [pairs](int64_t tiles) {
+    const int64_t waves = (tiles + pairs - 1) / pairs;
+    return static_cast<double>(tiles) / static_cast<double>(waves * pairs);
+  };
   const int64_t wide_pair_tiles = ((M + 255) / 256) * ((N + 511) / 512);
-  if (wide_pair_tiles >= kSms / 2) {
-    // 256 x 512 tiles on CTA pairs: A is loaded once for two 256-column
-    // halves, the least L2 traffic per FLOP in the bank.
+  const int64_t pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
+  // 256 x 512 tiles on CTA pairs: A is loaded once for two 256-column
+  // halves, the least L2 traffic per FLOP in the bank -- unless their last
+  // wave leaves many pairs idle and 256 x 256 tiles fill the waves better.
+  if (wide_pair_tiles >= pairs && !(wave_fill(wide_pair_tiles) < 0.93 && wave_fill(pair_tiles) > 0.97)) {
     int knobs[IDB_MENU_COLS] = {2 * kBM, 512, kBK, 4, 2, 1, 8, 1};
     return gemm_cfg_find(knobs, IDB_MENU_COLS);
   }
-  const int64_t pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
-  if (pair_tiles >= kSms / 2) {
+  if (pair_tiles >= pairs) {
     int knobs[IDB_MENU_COLS] = {2 * kBM, 256, kBK, 4, 2, 0, 8, 1};
     return gemm_cfg_find(knobs, IDB_MENU_COLS);
   }

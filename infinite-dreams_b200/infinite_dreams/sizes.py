@@ -40,6 +40,12 @@ def large_size() -> Shape:
     return (16384, 16384, 16384)
 
 
+def sharded_sizes() -> List[Shape]:
+    """Per-rank shapes of the 16384^3 GEMM row-sharded over 2, 4 and 8 ranks."""
+    n = large_size()[0]
+    return [(n // p, n, n) for p in (2, 4, 8)]
+
+
 def shape_sets() -> Dict[str, List[Shape]]:
     return {
         "single": single_sizes(),
@@ -47,5 +53,6 @@ def shape_sets() -> Dict[str, List[Shape]]:
         "skinny": skinny_sizes(),
         "irregular": irregular_sizes(),
         "large": [large_size()],
+        "sharded": sharded_sizes(),
         "default": default_sizes(),
     }
