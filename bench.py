@@ -364,24 +364,43 @@ def run_ours(args: argparse.Namespace) -> None:
     # optional all-gather of C row blocks (NCCL over NVLink), timed on its own
     allgather = None
     if world > 1 and args.allgather:
+        from infinite_dreams.sharded import sharded_gemm
+
         Cfull = torch.empty((size, N), device=dev, dtype=torch.float16)
-        for _ in range(2):
-            dist.all_gather_into_tensor(Cfull, C)
-        barrier()
-        s0 = torch.cuda.Event(enable_timing=True)
-        s1 = torch.cuda.Event(enable_timing=True)
-        s0.record(stream)
-        for _ in range(args.steps):
+        n_ag = max(1, min(args.steps, 20))
+
+        def timed(fn) -> float:
+            for _ in range(2):
+                fn()
+            barrier()
+            s0 = torch.cuda.Event(enable_timing=True)
+            s1 = torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            for _ in range(n_ag):
+                fn()
+            s1.record(stream)
+            torch.cuda.synchronize()
+            t = torch.tensor([s0.elapsed_time(s1)], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t[0]) / n_ag
+
+        def one_shot():
             step()
             dist.all_gather_into_tensor(Cfull, C)
-        s1.record(stream)
-        torch.cuda.synchronize()
-        t = torch.tensor([s0.elapsed_time(s1)], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_ag = float(t[0]) / args.steps
-        allgather = {"ms_per_step_gemm_plus_allgather": ms_ag,
-                     "value_with_allgather": 2.0 * size ** 3 / (ms_ag * 1e-3) / 1e12,
-                     "bytes_received_per_rank": (world - 1) * rows * N * 2}
+
+        def pipelined():
+            # row chunks: chunk c's all-gather overlaps chunk c+1's GEMM
+            sharded_gemm(A, B, M_total=size, gather=True, out=Cfull, chunks=4,
+                         compute=lambda a, b, o: ext.gemm_forward_cfg(
+                             a, b, dispatch.lookup(a.shape[0], b.shape[1], a.shape[1]), out=o))
+
+        ms_one = timed(one_shot)
+        ms_pipe = timed(pipelined)
+        allgather = {"ms_per_step_gemm_then_allgather": ms_one,
+                     "value_gemm_then_allgather": 2.0 * size ** 3 / (ms_one * 1e-3) / 1e12,
+                     "ms_per_step_pipelined_4_chunks": ms_pipe,
+                     "value_pipelined": 2.0 * size ** 3 / (ms_pipe * 1e-3) / 1e12,
+                     "bytes_received_per_rank": (world - 1) * rows * N * 2, "steps": n_ag}
         del Cfull
 
     # End to end through the public op.  Every step copies its own inputs from

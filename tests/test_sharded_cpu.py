@@ -49,8 +49,9 @@ def _worker(rank, world, port, M, N, K, q):
         r0, r1 = row_block(M, world, rank)
         local = sharded_gemm(A[r0:r1].contiguous(), B, compute=_cpu_compute)
         full = sharded_gemm(A[r0:r1].contiguous(), B, M_total=M, gather=True, compute=_cpu_compute)
+        piped = sharded_gemm(A[r0:r1].contiguous(), B, M_total=M, gather=True, compute=_cpu_compute, chunks=3)
         q.put((rank, local.numpy().view(np.uint16), full.numpy().view(np.uint16), (r0, r1),
-               oracle.gemm_f16(A.numpy(), B.numpy()).view(np.uint16)))
+               oracle.gemm_f16(A.numpy(), B.numpy()).view(np.uint16), piped.numpy().view(np.uint16)))
     finally:
         dist.destroy_process_group()
 
@@ -68,6 +69,8 @@ def test_two_rank_sharded_gemm_matches_single(M):
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    for rank, local, full, (r0, r1), ref in results:
+    for rank, local, full, (r0, r1), ref, piped in results:
         assert np.array_equal(local, ref[r0:r1])
         assert np.array_equal(full, ref)
+        # pipelined exchange (equal blocks) or its one-shot fallback (unequal)
+        assert np.array_equal(piped, ref)
