@@ -210,7 +210,7 @@ def run_reference(args: argparse.Namespace) -> None:
     bank = reference_cuda_bank(size, args.ref_shapes)
     if bank is not None:
         line["reference_cuda_bank"] = bank
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def reference_cuda_bank(size: int, all_shapes: bool) -> Optional[Dict[str, object]]:
@@ -389,8 +389,8 @@ def run_ours(args: argparse.Namespace) -> None:
             dist.all_gather_into_tensor(Cfull, C)
 
         def pipelined():
-            # row chunks: chunk c's all-gather overlaps chunk c+1's GEMM
-            sharded_gemm(A, B, M_total=size, gather=True, out=Cfull, chunks=4,
+            # two row chunks: the first chunk's all-gather overlaps the second chunk's GEMM
+            sharded_gemm(A, B, M_total=size, gather=True, out=Cfull, chunks=2,
                          compute=lambda a, b, o: ext.gemm_forward_cfg(
                              a, b, dispatch.lookup(a.shape[0], b.shape[1], a.shape[1]), out=o))
 
@@ -398,7 +398,7 @@ def run_ours(args: argparse.Namespace) -> None:
         ms_pipe = timed(pipelined)
         allgather = {"ms_per_step_gemm_then_allgather": ms_one,
                      "value_gemm_then_allgather": 2.0 * size ** 3 / (ms_one * 1e-3) / 1e12,
-                     "ms_per_step_pipelined_4_chunks": ms_pipe,
+                     "ms_per_step_pipelined_2_chunks": ms_pipe,
                      "value_pipelined": 2.0 * size ** 3 / (ms_pipe * 1e-3) / 1e12,
                      "bytes_received_per_rank": (world - 1) * rows * N * 2, "steps": n_ag}
         del Cfull
@@ -493,7 +493,7 @@ def run_ours(args: argparse.Namespace) -> None:
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps,
         "clocks": clocks, "allgather": allgather,
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def traffic_for(size: int, world: int) -> Optional[float]:
@@ -508,8 +508,27 @@ def traffic_for(size: int, world: int) -> Optional[float]:
         return None
 
 
+def _reserve_stdout_for_result() -> None:
+    """Keeps stdout for the one JSON line: libraries that write to file
+    descriptor 1 (NCCL prints its version there) go to stderr instead."""
+    global _RESULT_OUT
+    _RESULT_OUT = os.fdopen(os.dup(1), "w")
+    sys.stdout.flush()
+    os.dup2(2, 1)
+
+
+_RESULT_OUT = None
+
+
+def emit(line: Dict[str, object]) -> None:
+    out = _RESULT_OUT if _RESULT_OUT is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
 def main() -> None:
     args = parse()
+    _reserve_stdout_for_result()
     if args.impl == "reference":
         run_reference(args)
     else:
