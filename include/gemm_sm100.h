@@ -93,6 +93,37 @@ int gemm_launch_knobs(const void* A, const void* B, void* C, int64_t M, int64_t 
                       int64_t ldb, int64_t ldc, const int* knobs, int n, void* workspace,
                       size_t workspace_bytes, void* stream);
 
+/* Activations of the fused epilogue (gemm_launch_ex). */
+#define GEMM_ACT_NONE 0
+#define GEMM_ACT_RELU 1 /* max(x, 0)                                    */
+#define GEMM_ACT_GELU 2 /* x * Phi(x) = 0.5 x (1 + erf(x / sqrt(2)))    */
+
+/* C = act(alpha * op(A) * op(B) + beta * D + bias), rounded once to fp16.
+ *  op(A) = A (stored M x K, lda >= K) when trans_a = 0, or A^T with A stored
+ *          K x M (lda >= M) when trans_a = 1;
+ *  op(B) = B (stored K x N, ldb >= N) when trans_b = 0, or B^T with B stored
+ *          N x K (ldb >= K) when trans_b = 1;
+ *  D     = fp16 M x N with pitch ldd >= N; read only when beta != 0, and may
+ *          be C itself (in-place accumulate);
+ *  bias  = fp16[N] added to every row, or NULL; it must not overlap C;
+ *  activation = GEMM_ACT_*.
+ * The epilogue runs in fp32 on the fp32 accumulator.  With alpha = 1,
+ * beta = 0, no bias and no activation the result is exactly gemm_launch's.
+ * Transposed operands are read in place: the tensor cores take either major
+ * order from shared memory, so no transposed copy is made.  Any cfg_id
+ * serves every layout; the workspace comes from gemm_workspace_bytes_ex.
+ * Extends gemm_launch beyond the reference, whose op took only row-major
+ * A and B (made contiguous first, src/gemm_ext.cpp:89-90) and returned A*B. */
+int gemm_launch_ex(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                   int64_t ldb, int64_t ldc, int trans_a, int trans_b, float alpha, float beta, const void* D,
+                   int64_t ldd, const void* bias, int activation, int cfg_id, void* workspace,
+                   size_t workspace_bytes, void* stream);
+
+/* Workspace bytes gemm_launch_ex needs (operands stored as trans_a/trans_b
+ * say); gemm_workspace_bytes is this with trans_a = trans_b = 0. */
+size_t gemm_workspace_bytes_ex(const void* A, const void* B, int64_t M, int64_t N, int64_t K, int64_t lda,
+                               int64_t ldb, int trans_a, int trans_b, int cfg_id);
+
 /* A reasonable configuration for a shape when no tuned entry exists.
  * No counterpart in the reference (its tuner had no per-shape dispatch). */
 int gemm_default_cfg(int64_t M, int64_t N, int64_t K);

@@ -67,6 +67,20 @@ __global__ void pack_rows_f16(const __half* __restrict__ src, long long lds, __h
 }
 
 
+// C = act(beta * D + bias) for an empty reduction (K = 0) with a fused
+// epilogue: the accumulator is 0, so alpha plays no part.
+__global__ void epilogue_only_f16(GemmParams p) {
+  const long long total = static_cast<long long>(p.M) * p.N;
+  for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = idx / p.N;
+    const int c = static_cast<int>(idx - r * p.N);
+    const float d = (p.beta != 0.0f) ? __half2float(p.D[r * p.ldd + c]) : 0.0f;
+    const float b = (p.bias != nullptr) ? __half2float(p.bias[c]) : 0.0f;
+    p.C[r * p.ldc + c] = __float2half_rn(epilogue_value(p, 0.0f, d, b));
+  }
+}
+
 enum MenuCol { kColTileM = 0, kColTileN, kColTileK, kColStages, kColMmaSm, kColRaster, kColGroup, kColSplitK };
 
 __device__ int g_device_error = 0;
@@ -156,8 +170,20 @@ constexpr size_t kCounterBytes = static_cast<size_t>(kCounterSlots) * sizeof(uns
 // iterations are split evenly over W workers (same formula as the kernel).
 int64_t sk_owner(int64_t x, int64_t T, int64_t W) { return ((x + 1) * W - 1) / T; }
 
+// How the operands are stored and what the epilogue computes (gemm_launch_ex).
+struct OpDesc {
+  int trans_a = 0;  // 0: A stored M x K; 1: A stored K x M
+  int trans_b = 0;  // 0: B stored K x N; 1: B stored N x K
+  float alpha = 1.0f, beta = 0.0f;
+  const void* D = nullptr;
+  int64_t ldd = 0;
+  const void* bias = nullptr;
+  int act = 0;
+  bool epi() const { return alpha != 1.0f || beta != 0.0f || bias != nullptr || act != 0; }
+};
+
 int make_plan(const void* A, const void* B, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
-              int cfg_id, int sms, Plan* pl) {
+              int trans_a, int trans_b, int cfg_id, int sms, Plan* pl) {
   if (cfg_id < 0 || cfg_id >= IDB_MENU_SIZE) {
     return fail(GEMM_ERR_BAD_CFG, "cfg_id " + std::to_string(cfg_id) + " out of range [0, " +
                                       std::to_string(IDB_MENU_SIZE) + ")");
@@ -213,16 +239,17 @@ int make_plan(const void* A, const void* B, int64_t M, int64_t N, int64_t K, int
     off += static_cast<size_t>(pl->num_tiles) * pl->max_parts * kBM * pl->tile_n * sizeof(float);
     off = static_cast<size_t>(round_up(static_cast<int64_t>(off), 256));
   }
+  // A packed copy keeps the operand's stored orientation (rows x cols below).
   if (pl->pack_a) {
-    pl->lda_packed = round_up(K, 8);
+    pl->lda_packed = round_up(trans_a ? M : K, 8);
     pl->off_pack_a = off;
-    off += static_cast<size_t>(M) * pl->lda_packed * 2;
+    off += static_cast<size_t>(trans_a ? K : M) * pl->lda_packed * 2;
     off = static_cast<size_t>(round_up(static_cast<int64_t>(off), 256));
   }
   if (pl->pack_b) {
-    pl->ldb_packed = round_up(N, 8);
+    pl->ldb_packed = round_up(trans_b ? K : N, 8);
     pl->off_pack_b = off;
-    off += static_cast<size_t>(K) * pl->ldb_packed * 2;
+    off += static_cast<size_t>(trans_b ? N : K) * pl->ldb_packed * 2;
     off = static_cast<size_t>(round_up(static_cast<int64_t>(off), 256));
   }
   pl->total = off;
@@ -305,16 +332,30 @@ int launch_pack(const void* src, int64_t lds, void* dst, int64_t ldd, int64_t ro
 }
 
 int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
-                int64_t ldc, int cfg_id, void* ws, size_t ws_bytes, void* stream_v) {
+                int64_t ldc, const OpDesc& op, int cfg_id, void* ws, size_t ws_bytes, void* stream_v) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
   if (M < 0 || N < 0 || K < 0) return fail(GEMM_ERR_INVALID_ARG, "M, N, K must be >= 0");
+  if ((op.trans_a != 0 && op.trans_a != 1) || (op.trans_b != 0 && op.trans_b != 1)) {
+    return fail(GEMM_ERR_INVALID_ARG, "trans_a and trans_b must be 0 or 1");
+  }
+  if (op.act < GEMM_ACT_NONE || op.act > GEMM_ACT_GELU) {
+    return fail(GEMM_ERR_INVALID_ARG, "activation must be GEMM_ACT_NONE, GEMM_ACT_RELU or GEMM_ACT_GELU");
+  }
   if (M == 0 || N == 0) return GEMM_OK;
   if (!C || (K > 0 && (!A || !B))) return fail(GEMM_ERR_INVALID_ARG, "A, B and C must be non-null");
-  if (lda < K || ldb < N || ldc < N) {
-    return fail(GEMM_ERR_INVALID_ARG, "pitches must satisfy lda >= K, ldb >= N, ldc >= N");
+  const int64_t a_cols = op.trans_a ? M : K, b_cols = op.trans_b ? K : N;
+  if (lda < a_cols || ldb < b_cols || ldc < N) {
+    return fail(GEMM_ERR_INVALID_ARG, std::string("pitches must satisfy lda >= ") + (op.trans_a ? "M" : "K") +
+                                          ", ldb >= " + (op.trans_b ? "K" : "N") + ", ldc >= N");
   }
   if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) | reinterpret_cast<uintptr_t>(C)) % 2u) {
     return fail(GEMM_ERR_INVALID_ARG, "A, B and C must be 2-byte aligned (fp16)");
+  }
+  if (op.beta != 0.0f && (!op.D || op.ldd < N || reinterpret_cast<uintptr_t>(op.D) % 2u)) {
+    return fail(GEMM_ERR_INVALID_ARG, "beta != 0 needs a 2-byte aligned D with ldd >= N");
+  }
+  if (op.bias && reinterpret_cast<uintptr_t>(op.bias) % 2u) {
+    return fail(GEMM_ERR_INVALID_ARG, "bias must be 2-byte aligned (fp16)");
   }
   if (cfg_id < 0 || cfg_id >= IDB_MENU_SIZE) {
     return fail(GEMM_ERR_BAD_CFG, "cfg_id " + std::to_string(cfg_id) + " out of range [0, " +
@@ -324,10 +365,35 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
   int st = device_info(&dinfo);
   if (st != GEMM_OK) return st;
   Plan pl;
-  st = make_plan(A, B, M, N, K, lda, ldb, cfg_id, dinfo.sms, &pl);
+  st = make_plan(A, B, M, N, K, lda, ldb, op.trans_a, op.trans_b, cfg_id, dinfo.sms, &pl);
   if (st != GEMM_OK) return st;
+
+  GemmParams p;
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.C = static_cast<__half*>(C);
+  p.ldc = ldc;
+  p.a_mn = op.trans_a;
+  p.b_kmaj = op.trans_b;
+  p.epi = op.epi() ? 1 : 0;
+  p.act = op.act;
+  p.alpha = op.alpha;
+  p.beta = op.beta;
+  p.D = op.beta != 0.0f ? static_cast<const __half*>(op.D) : nullptr;
+  p.ldd = op.beta != 0.0f ? op.ldd : 0;
+  p.bias = static_cast<const __half*>(op.bias);
   if (K == 0) {
-    // Empty reduction: C = 0 (the reference kernel's loop body never runs).
+    // Empty reduction: C = 0 (the reference kernel's loop body never runs),
+    // or act(beta * D + bias) with a fused epilogue.
+    if (p.epi) {
+      const long long total = M * N;
+      long long blocks = (total + 255) / 256;
+      if (blocks > 148 * 8) blocks = 148 * 8;
+      epilogue_only_f16<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(p);
+      cudaError_t e = cudaGetLastError();
+      return e == cudaSuccess ? GEMM_OK : fail_cuda(e, "epilogue_only_f16 launch");
+    }
     cudaError_t e = cudaMemset2DAsync(C, static_cast<size_t>(ldc) * 2, 0, static_cast<size_t>(N) * 2,
                                       static_cast<size_t>(M), stream);
     return e == cudaSuccess ? GEMM_OK : fail_cuda(e, "cudaMemset2DAsync");
@@ -351,13 +417,13 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
   const void* b_src = B;
   int64_t b_ld = ldb;
   if (pl.pack_a) {
-    st = launch_pack(A, lda, wsb + pl.off_pack_a, pl.lda_packed, M, K, stream);
+    st = launch_pack(A, lda, wsb + pl.off_pack_a, pl.lda_packed, op.trans_a ? K : M, op.trans_a ? M : K, stream);
     if (st != GEMM_OK) return st;
     a_src = wsb + pl.off_pack_a;
     a_ld = pl.lda_packed;
   }
   if (pl.pack_b) {
-    st = launch_pack(B, ldb, wsb + pl.off_pack_b, pl.ldb_packed, K, N, stream);
+    st = launch_pack(B, ldb, wsb + pl.off_pack_b, pl.ldb_packed, op.trans_b ? N : K, op.trans_b ? K : N, stream);
     if (st != GEMM_OK) return st;
     b_src = wsb + pl.off_pack_b;
     b_ld = pl.ldb_packed;
@@ -365,9 +431,19 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
 
   CUtensorMap tmA, tmB, tmC;
   std::memset(&tmC, 0, sizeof(tmC));
-  st = encode_2d_cached(&tmA, a_src, K, M, a_ld, kBK, kBM, "A");
+  // Boxes: K-major A [64 K x 128 rows]; M-major A, and B either way, in
+  // 64 x 64 atoms (see the producer in gemm_sm100_kernel.cuh).
+  if (op.trans_a) {
+    st = encode_2d_cached(&tmA, a_src, M, K, a_ld, 64, kBK, "A (stored K x M)");
+  } else {
+    st = encode_2d_cached(&tmA, a_src, K, M, a_ld, kBK, kBM, "A");
+  }
   if (st != GEMM_OK) return st;
-  st = encode_2d_cached(&tmB, b_src, N, K, b_ld, 64, kBK, "B");
+  if (op.trans_b) {
+    st = encode_2d_cached(&tmB, b_src, K, N, b_ld, kBK, 64, "B (stored N x K)");
+  } else {
+    st = encode_2d_cached(&tmB, b_src, N, K, b_ld, 64, kBK, "B");
+  }
   if (st != GEMM_OK) return st;
   const bool c_tma = tma_addressable(C, ldc);
   if (c_tma) {
@@ -384,10 +460,6 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
   if (g_err_status[dev] != cudaSuccess) return fail_cuda(g_err_status[dev], "cudaGetSymbolAddress(g_device_error)");
   int* err_word = g_err_word[dev];
 
-  GemmParams p;
-  p.M = static_cast<int>(M);
-  p.N = static_cast<int>(N);
-  p.K = static_cast<int>(K);
   p.tiles_m = pl.tiles_m;
   p.tiles_n = pl.tiles_n;
   p.num_tiles = pl.num_tiles;
@@ -399,8 +471,6 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
   p.raster = pl.raster;
   p.group = pl.group;
   p.c_tma = c_tma ? 1 : 0;
-  p.C = static_cast<__half*>(C);
-  p.ldc = ldc;
   p.partials = pl.max_parts > 1 ? reinterpret_cast<float*>(wsb + pl.off_partials) : nullptr;
   p.counters = pl.max_parts > 1 ? reinterpret_cast<unsigned int*>(wsb) : nullptr;
   p.err = err_word;
@@ -455,8 +525,8 @@ int gemm_cfg_find(const int* knobs, int n) {
   return -1;
 }
 
-size_t gemm_workspace_bytes(const void* A, const void* B, int64_t M, int64_t N, int64_t K, int64_t lda,
-                            int64_t ldb, int cfg_id) {
+size_t gemm_workspace_bytes_ex(const void* A, const void* B, int64_t M, int64_t N, int64_t K, int64_t lda,
+                               int64_t ldb, int trans_a, int trans_b, int cfg_id) {
   Plan pl;
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   // Stream-K workspace depends on the SM count of the current device (148
@@ -469,8 +539,13 @@ size_t gemm_workspace_bytes(const void* A, const void* B, int64_t M, int64_t N, 
     cudaGetLastError();
     t_last_error.clear();
   }
-  if (make_plan(A, B, M, N, K, lda, ldb, cfg_id, sms, &pl) != GEMM_OK) return 0;
+  if (make_plan(A, B, M, N, K, lda, ldb, trans_a, trans_b, cfg_id, sms, &pl) != GEMM_OK) return 0;
   return pl.total;
+}
+
+size_t gemm_workspace_bytes(const void* A, const void* B, int64_t M, int64_t N, int64_t K, int64_t lda,
+                            int64_t ldb, int cfg_id) {
+  return gemm_workspace_bytes_ex(A, B, M, N, K, lda, ldb, 0, 0, cfg_id);
 }
 
 size_t gemm_workspace_counter_bytes(void) { return kCounterBytes; }
@@ -478,7 +553,24 @@ size_t gemm_workspace_counter_bytes(void) { return kCounterBytes; }
 int gemm_launch(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
                 int64_t ldc, int cfg_id, void* workspace, size_t workspace_bytes, void* stream) {
   t_last_error.clear();
-  return launch_impl(A, B, C, M, N, K, lda, ldb, ldc, cfg_id, workspace, workspace_bytes, stream);
+  return launch_impl(A, B, C, M, N, K, lda, ldb, ldc, OpDesc{}, cfg_id, workspace, workspace_bytes, stream);
+}
+
+int gemm_launch_ex(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                   int64_t ldb, int64_t ldc, int trans_a, int trans_b, float alpha, float beta, const void* D,
+                   int64_t ldd, const void* bias, int activation, int cfg_id, void* workspace,
+                   size_t workspace_bytes, void* stream) {
+  t_last_error.clear();
+  OpDesc op;
+  op.trans_a = trans_a;
+  op.trans_b = trans_b;
+  op.alpha = alpha;
+  op.beta = beta;
+  op.D = D;
+  op.ldd = ldd;
+  op.bias = bias;
+  op.act = activation;
+  return launch_impl(A, B, C, M, N, K, lda, ldb, ldc, op, cfg_id, workspace, workspace_bytes, stream);
 }
 
 int gemm_launch_knobs(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
@@ -491,7 +583,7 @@ int gemm_launch_knobs(const void* A, const void* B, void* C, int64_t M, int64_t 
     for (int i = 0; knobs && i < n; ++i) t += (i ? "," : "") + std::to_string(knobs[i]);
     return fail(GEMM_ERR_BAD_CFG, "knob tuple " + t + ") is not in the kernel bank menu");
   }
-  return launch_impl(A, B, C, M, N, K, lda, ldb, ldc, id, workspace, workspace_bytes, stream);
+  return launch_impl(A, B, C, M, N, K, lda, ldb, ldc, OpDesc{}, id, workspace, workspace_bytes, stream);
 }
 
 int gemm_default_cfg(int64_t M, int64_t N, int64_t K) {

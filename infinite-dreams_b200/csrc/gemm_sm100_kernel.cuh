@@ -5,15 +5,19 @@
 // fp32 accumulate, fp16 out rounded to nearest as __float2half does, zero
 // contribution from rows/columns outside M/N/K), built the Blackwell way:
 //
-//   warp 0      TMA producer: A box [128 x 64] (K-major, 128B swizzle) and
-//               B boxes [64 x 64] (N-major, 128B swizzle) per pipeline stage,
-//               completing on a `full` mbarrier.
+//   warp 0      TMA producer: per pipeline stage one A tile [128 rows x 64 K]
+//               and one B tile [64 K x BN/CG columns], 128B-swizzled, in
+//               whichever major order the operand is stored (row-major A is
+//               K-major, a stored-transposed A is M-major; row-major B is
+//               N-major, a stored-transposed B is K-major), completing on a
+//               `full` mbarrier.
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
 //               (K=16 per instruction), frees smem stages with
 //               tcgen05.commit -> `empty` mbarrier, hands finished accumulators
 //               to the epilogue with tcgen05.commit -> `tmem_full`.
-//   warps 2..5  epilogue: tcgen05.ld (32 lanes x 32 columns per warp), fp16
-//               conversion, 128B-swizzled smem staging, TMA store (or a
+//   warps 2..5  epilogue: tcgen05.ld (32 lanes x 32 columns per warp), the
+//               optional fused alpha / beta*D / bias / activation step in
+//               fp32, fp16 conversion, 128B-swizzled smem staging, TMA store (or a
 //               coalesced st.global path when C's row pitch is not 16-byte
 //               aligned).  Split-K / stream-K partials go to an fp32
 //               workspace; the last CTA of a tile (atomic ticket, no
@@ -64,6 +68,20 @@ struct GemmParams {
   float* partials;          // fp32 partial tiles (tile, part, 128 x BN) of split-K / stream-K
   unsigned int* counters;   // split-K tickets, zero on entry and on exit
   int* err;                 // device error word
+  // Operand layouts.  a_mn = 1: A is stored K x M (the GEMM uses its
+  // transpose), its tiles are loaded M-major; b_kmaj = 1: B is stored N x K,
+  // its tiles are loaded K-major.  tcgen05 reads either major order from
+  // shared memory, so no operand is ever transposed in memory.
+  int a_mn, b_kmaj;
+  // Fused epilogue (epi = 1):  C = act(alpha * acc + beta * D + bias[col]),
+  // evaluated in fp32 and rounded once to fp16.  D is read only when
+  // beta != 0 and may be C itself; bias (fp16[N]) may be null.
+  // act: 0 none, 1 ReLU, 2 GELU (erf form).  epi = 0: C = fp16(acc).
+  int epi, act;
+  float alpha, beta;
+  const __half* D;
+  long long ldd;
+  const __half* bias;
 };
 
 template <int BN, int STAGES, int CG>
@@ -193,6 +211,65 @@ __device__ __forceinline__ bool work_next(const GemmParams& p, int worker, int w
   return true;
 }
 
+__device__ __forceinline__ float apply_act(float x, int act) {
+  if (act == 1) return fmaxf(x, 0.0f);
+  if (act == 2) return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));  // x * Phi(x)
+  return x;
+}
+
+// One element of the fused epilogue; d and b are the D and bias values.
+__device__ __forceinline__ float epilogue_value(const GemmParams& p, float acc, float d, float b) {
+  float v = p.alpha * acc;
+  if (p.beta != 0.0f) v = fmaf(p.beta, d, v);
+  return apply_act(v + b, p.act);
+}
+
+// 64 consecutive fp16 values src[0..63] as 8 x 16 bytes; positions at or
+// past `valid` read as 0.  `vec`: src is 16-byte aligned.  Plain (coherent)
+// loads, because D may be the C that this kernel writes.
+__device__ __forceinline__ void load_chunk64(const __half* src, int valid, bool vec, uint4 (&out)[8]) {
+  if (vec && valid >= 64) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) out[q] = __ldcg(reinterpret_cast<const uint4*>(src) + q);
+  } else {
+    const unsigned short* s = reinterpret_cast<const unsigned short*>(src);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      unsigned short h[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) h[e] = (8 * q + e < valid) ? s[8 * q + e] : static_cast<unsigned short>(0);
+      out[q] = make_uint4(h[0] | (static_cast<uint32_t>(h[1]) << 16), h[2] | (static_cast<uint32_t>(h[3]) << 16),
+                          h[4] | (static_cast<uint32_t>(h[5]) << 16), h[6] | (static_cast<uint32_t>(h[7]) << 16));
+    }
+  }
+}
+
+__device__ __forceinline__ float half_lo(uint32_t w) { return __low2float(*reinterpret_cast<const __half2*>(&w)); }
+__device__ __forceinline__ float half_hi(uint32_t w) { return __high2float(*reinterpret_cast<const __half2*>(&w)); }
+
+// Applies the fused epilogue to the 64 values of one row chunk (columns
+// col0 .. col0 + 63 of C); dv holds the row's D values (unused when beta = 0).
+__device__ __forceinline__ void apply_epilogue64(const GemmParams& p, float (&f)[64], const uint4 (&dv)[8], int col0) {
+  uint4 bv[8];
+  if (p.bias != nullptr) {
+    const bool vec = (reinterpret_cast<uintptr_t>(p.bias) & 15u) == 0;
+    load_chunk64(p.bias + col0, p.N - col0, vec, bv);
+  } else {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) bv[q] = make_uint4(0u, 0u, 0u, 0u);
+  }
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const uint32_t dw[4] = {dv[q].x, dv[q].y, dv[q].z, dv[q].w};
+    const uint32_t bw[4] = {bv[q].x, bv[q].y, bv[q].z, bv[q].w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      f[8 * q + 2 * e] = epilogue_value(p, f[8 * q + 2 * e], half_lo(dw[e]), half_lo(bw[e]));
+      f[8 * q + 2 * e + 1] = epilogue_value(p, f[8 * q + 2 * e + 1], half_hi(dw[e]), half_hi(bw[e]));
+    }
+  }
+}
+
 // Reduction of a split tile by the 128 epilogue threads of the CTA that
 // brought its last K piece: C[row0 + r][col0 + c] = sum over parts (in K
 // order) of the fp32 partial slots, for the tile's valid rows/columns.  The
@@ -243,6 +320,14 @@ __device__ __forceinline__ void reduce_partials(const GemmParams& p, const float
       if (e >= E) continue;
       const int r = e % R, j4 = e / R;
       const int gc = col0 + 4 * j4;
+      if (p.epi) {
+        float* v = &acc[b].x;
+        for (int c = 0; c < 4 && gc + c < p.N; ++c) {
+          const float d = (p.beta != 0.0f) ? __half2float(p.D[static_cast<long long>(row0 + r) * p.ldd + gc + c]) : 0.0f;
+          const float bb = (p.bias != nullptr) ? __half2float(p.bias[gc + c]) : 0.0f;
+          v[c] = epilogue_value(p, v[c], d, bb);
+        }
+      }
       __half* dst = p.C + static_cast<long long>(row0 + r) * p.ldc + gc;
       if (vec && gc + 3 < p.N) {
         uint2 hv;
@@ -360,21 +445,39 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           }
           uint8_t* a_dst = sA + stage * Plan::kABytes;
           uint8_t* b_dst = sB + stage * Plan::kBBytes;
+          // Tiles land in the canonical 128-byte-swizzled layouts: K-major A
+          // is one [128 rows x 64 K] box; M-major A is two [64 K x 64 M]
+          // atoms; B is kBNc/64 atoms of 64 columns, [64 K x 64 N] boxes when
+          // N-major, [64 N x 64 K] boxes when K-major.  (x, y) = (inner, outer)
+          // coordinates of the operand as stored.
+          const int k0 = kb * kBK;
           if constexpr (CG == 1) {
             mbar_arrive_expect_tx(&full_bar[stage], Plan::kStageBytes);
-            tma_load_2d(a_dst, &tmA, &full_bar[stage], kb * kBK, arow);
+            if (!p.a_mn) {
+              tma_load_2d(a_dst, &tmA, &full_bar[stage], k0, arow);
+            } else {
+              tma_load_2d(a_dst, &tmA, &full_bar[stage], arow, k0);
+              tma_load_2d(a_dst + kBK * 128, &tmA, &full_bar[stage], arow + 64, k0);
+            }
 #pragma unroll
             for (int j = 0; j < kBNc / 64; ++j) {
-              tma_load_2d(b_dst + j * (kBK * 128), &tmB, &full_bar[stage], bcol + b_atom_col<Plan>(j), kb * kBK);
+              const int n = bcol + b_atom_col<Plan>(j);
+              tma_load_2d(b_dst + j * (kBK * 128), &tmB, &full_bar[stage], p.b_kmaj ? k0 : n, p.b_kmaj ? n : k0);
             }
           } else {
             // Both CTAs' bytes complete on the even CTA's `full` barrier.
             if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * Plan::kStageBytes);
             const uint32_t bar = mapa_shared(smem_u32(&full_bar[stage]), 0);
-            tma_load_2d_pair(a_dst, &tmA, bar, kb * kBK, arow);
+            if (!p.a_mn) {
+              tma_load_2d_pair(a_dst, &tmA, bar, k0, arow);
+            } else {
+              tma_load_2d_pair(a_dst, &tmA, bar, arow, k0);
+              tma_load_2d_pair(a_dst + kBK * 128, &tmA, bar, arow + 64, k0);
+            }
 #pragma unroll
             for (int j = 0; j < kBNc / 64; ++j) {
-              tma_load_2d_pair(b_dst + j * (kBK * 128), &tmB, bar, bcol + b_atom_col<Plan>(j), kb * kBK);
+              const int n = bcol + b_atom_col<Plan>(j);
+              tma_load_2d_pair(b_dst + j * (kBK * 128), &tmB, bar, p.b_kmaj ? k0 : n, p.b_kmaj ? n : k0);
             }
           }
           ++issued;
@@ -411,7 +514,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && leader) {
-      constexpr uint32_t idesc = idesc_f16_f32(kBM * CG, Plan::kMmaN, /*a_mn_major=*/false, /*b_mn_major=*/true);
+      const uint32_t idesc = idesc_f16_f32(kBM * CG, Plan::kMmaN, p.a_mn != 0, p.b_kmaj == 0);
+      // Descriptor strides of the two major orders (128-byte swizzle):
+      //  K-major:  rows of 128 B, 8-row groups 1024 B apart, a K step of 16
+      //            elements advances 32 B inside the swizzled row;
+      //  MN-major: 64-element atoms kBK*128 B apart (LBO), 8-row K groups
+      //            1024 B apart (SBO), a K step advances 16 rows = 2 KiB.
+      const uint32_t a_lbo = p.a_mn ? kBK * 128 : 16, a_kstep = p.a_mn ? kUmmaK * 128 : kUmmaK * 2;
+      const uint32_t b_lbo = p.b_kmaj ? 16 : kBK * 128, b_kstep = p.b_kmaj ? kUmmaK * 2 : kUmmaK * 128;
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -445,13 +555,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           const uint32_t a0 = smem_u32(sA + stage * Plan::kABytes);
           const uint32_t b0 = smem_u32(sB + stage * Plan::kBBytes);
           // MMA i reads this CTA's atoms [i*kMmaNc/64, (i+1)*kMmaNc/64) and
-          // writes accumulator columns [i*kMmaN, (i+1)*kMmaN).  A: K-major,
-          // 16 elements (32 B) per K step inside the swizzled row; B: N-major,
-          // 16 K-rows (2 KiB) per K step, 64-column atoms kBK*128 B apart.
+          // writes accumulator columns [i*kMmaN, (i+1)*kMmaN).
           auto issue = [&](int i, int j) {
-            const uint64_t ad = smem_desc_sw128(a0 + j * (kUmmaK * 2), 16, 1024);
-            const uint64_t bd = smem_desc_sw128(b0 + i * (Plan::kMmaNc / 64) * (kBK * 128) + j * (kUmmaK * 128),
-                                                kBK * 128, 1024);
+            const uint64_t ad = smem_desc_sw128(a0 + j * a_kstep, a_lbo, 1024);
+            const uint64_t bd =
+                smem_desc_sw128(b0 + i * (Plan::kMmaNc / 64) * (kBK * 128) + j * b_kstep, b_lbo, 1024);
             mma_f16_ss<CG>(d_tmem + static_cast<uint32_t>(i * Plan::kMmaN), ad, bd, idesc,
                            (kb > kb0 || j > 0) ? 1u : 0u);
           };
@@ -587,6 +695,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       {
 #pragma unroll 1
         for (int c64 = 0; c64 < BN / 64; ++c64) {
+          const int col0 = tn * BN + c64 * 64;
+          // D for this row chunk: issued before the TMEM reads so that its
+          // latency overlaps them
+          uint4 dv[8];
+          if (p.epi && p.beta != 0.0f && row_ok && col0 < p.N) {
+            const __half* drow = p.D + static_cast<long long>(grow) * p.ldd + col0;
+            load_chunk64(drow, p.N - col0, (reinterpret_cast<uintptr_t>(drow) & 15u) == 0, dv);
+          } else {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) dv[q] = make_uint4(0u, 0u, 0u, 0u);
+          }
           float f[64];
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
@@ -623,13 +742,13 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 #pragma unroll
             for (int i = 0; i < 64; ++i) f[i] = s[i];
           }
+          if (p.epi && col0 < p.N) apply_epilogue64(p, f, dv, col0);
           uint8_t* buf = cbufs + cb * Plan::kCBufBytes;
           if (p.c_tma) {
             if (lane == 0) bulk_wait_group_read<1>();
             __syncwarp();
           }
           stage_row_sw128(buf, lane, f);
-          const int col0 = tn * BN + c64 * 64;
           const int row0 = cta_row0 + ew * 32;
           if (p.c_tma) {
             fence_proxy_async_smem();

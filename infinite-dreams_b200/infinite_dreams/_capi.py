@@ -20,6 +20,11 @@ GEMM_ERR_CUDA = 4
 GEMM_ERR_UNSUPPORTED = 5
 GEMM_ERR_DEVICE_TIMEOUT = 6
 
+GEMM_ACT_NONE = 0
+GEMM_ACT_RELU = 1
+GEMM_ACT_GELU = 2
+ACTIVATIONS = {"none": GEMM_ACT_NONE, "relu": GEMM_ACT_RELU, "gelu": GEMM_ACT_GELU}
+
 # (name, restype, argtypes) of every exported entry point.
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
@@ -37,6 +42,11 @@ _SIG = [
      [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, ctypes.POINTER(ctypes.c_int), ctypes.c_int, _P,
       ctypes.c_size_t, _P]),
     ("gemm_launch_noalloc", ctypes.c_int, [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, ctypes.c_int, _P]),
+    ("gemm_launch_ex", ctypes.c_int,
+     [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_float,
+      _P, _I64, _P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_size_t, _P]),
+    ("gemm_workspace_bytes_ex", ctypes.c_size_t,
+     [_P, _P, _I64, _I64, _I64, _I64, _I64, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
     ("gemm_default_cfg", ctypes.c_int, [_I64, _I64, _I64]),
     ("gemm_device_error", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
     ("gemm_last_error", ctypes.c_char_p, []),

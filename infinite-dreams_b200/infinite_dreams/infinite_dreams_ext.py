@@ -15,6 +15,9 @@ by the sm_100a kernel bank through its C ABI (include/gemm_sm100.h):
 * ``gemm_cfg_table_cpu()`` -- the menu as a CPU int32 tensor
   ``[num_cfg, len(CFG_COLUMNS)]`` (src/gemm_ext.cpp:108-120).
 
+``gemm_ex`` goes beyond the reference: transposed operand views read in
+place and a fused epilogue (alpha, beta * C, bias, ReLU / GELU).
+
 Like the reference, inputs are made contiguous, C is allocated from torch's
 caching allocator on A's device, and the launch is asynchronous on the
 current stream.  Split-K / repacking workspace is cached per (device, stream)
@@ -139,6 +142,80 @@ def gemm_forward_cfg(A: torch.Tensor, B: torch.Tensor, cfg_id: int, *,
     return _launch(A, B, int(cfg_id), out)
 
 
+def _operand(X: torch.Tensor) -> Tuple[torch.Tensor, int, int]:
+    """(tensor, trans, pitch) for a logical [R, C] operand read in place.
+
+    A row-major view (unit column stride) is passed as stored; a transposed
+    view (unit row stride, e.g. ``W.t()``) is passed as its K-major storage
+    with trans = 1, which the kernels read without a copy.  Anything else is
+    made contiguous first.
+    """
+    R, C = X.shape
+    s0, s1 = X.stride()
+    if (s1 == 1 or C <= 1) and s0 >= max(C, 1):
+        return X, 0, s0
+    if (s0 == 1 or R <= 1) and s1 >= max(R, 1):
+        return X, 1, s1
+    X = X.contiguous()
+    return X, 0, max(C, 1)
+
+
+def gemm_ex(A: torch.Tensor, B: torch.Tensor, *, alpha: float = 1.0, beta: float = 0.0,
+            C: Optional[torch.Tensor] = None, bias: Optional[torch.Tensor] = None, activation: str = "none",
+            cfg_id: Optional[int] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out = act(alpha * A @ B + beta * C + bias), fp16, fused into the GEMM's epilogue.
+
+    A is a logical [M, K] and B a logical [K, N] fp16 CUDA tensor; row-major
+    and transposed views (``x.t()``) are read in place (gemm_launch_ex's
+    trans flags), other strides are copied.  C ([M, N], read only when
+    beta != 0) may be ``out`` itself for an in-place update; bias is [N].
+    activation: "none", "relu" or "gelu" (erf form).  cfg_id defaults to the
+    per-shape dispatch table entry, else the heuristic.
+    """
+    _check_inputs(A, B)
+    if activation not in _capi.ACTIVATIONS:
+        raise RuntimeError(f"activation must be one of {sorted(_capi.ACTIVATIONS)}")
+    M, K = A.shape
+    N = B.shape[1]
+    dev = A.device
+    if beta != 0.0:
+        if C is None:
+            raise RuntimeError("beta != 0 needs C")
+        if C.dtype != torch.float16 or tuple(C.shape) != (M, N) or C.device != dev:
+            raise RuntimeError("C must be a float16 (M x N) tensor on A's device")
+        if C.stride(1) != 1 and N > 1:
+            C = C.contiguous()
+    if bias is not None:
+        if bias.dtype != torch.float16 or bias.numel() != N or bias.device != dev:
+            raise RuntimeError("bias must be a float16 tensor of N elements on A's device")
+        bias = bias.reshape(N).contiguous()
+    if cfg_id is None:
+        from . import dispatch
+        cfg_id = dispatch.lookup(M, N, K)
+    elif not 0 <= int(cfg_id) < NUM_CFG:
+        raise RuntimeError("cfg_id out of range")
+    with torch.cuda.device(dev):
+        A_s, ta, lda = _operand(A)
+        B_s, tb, ldb = _operand(B)
+        if out is None:
+            out = torch.empty((M, N), dtype=torch.float16, device=dev)
+        elif (out.dtype != torch.float16 or tuple(out.shape) != (M, N) or out.device != dev
+              or (out.stride(1) != 1 and N > 1)):
+            raise RuntimeError("out must be a float16 (M x N) tensor with unit column stride on A's device")
+        stream = torch.cuda.current_stream(dev)
+        a_ptr, b_ptr = A_s.data_ptr(), B_s.data_ptr()
+        need = lib.gemm_workspace_bytes_ex(a_ptr, b_ptr, M, N, K, lda, ldb, ta, tb, int(cfg_id))
+        ws_ptr, ws_len = _workspace(dev, stream, need) if need else (0, 0)
+        d_ptr, ldd = (C.data_ptr(), max(C.stride(0), N)) if beta != 0.0 else (None, 0)
+        st = lib.gemm_launch_ex(a_ptr, b_ptr, out.data_ptr(), M, N, K, lda, ldb, max(out.stride(0), N), ta, tb,
+                                float(alpha), float(beta), d_ptr, ldd,
+                                bias.data_ptr() if bias is not None else None, _capi.ACTIVATIONS[activation],
+                                int(cfg_id), ws_ptr or None, ws_len, stream.cuda_stream or None)
+        if st:
+            _capi.check(st, "gemm_launch_ex")
+    return out
+
+
 def gemm_cfg_table_cpu() -> torch.Tensor:
     """CPU int32 tensor [num_cfg, len(CFG_COLUMNS)], columns CFG_COLUMNS."""
     cols, rows = _capi.menu()
@@ -159,5 +236,5 @@ def check_device_errors(device: Optional[int] = None) -> None:
         raise GemmError(st, f"device {dev}: kernel error bits {code.value}")
 
 
-__all__ = ["gemm_forward", "gemm_forward_cfg", "gemm_cfg_table_cpu", "CFG_COLUMNS", "NUM_CFG",
+__all__ = ["gemm_forward", "gemm_forward_cfg", "gemm_ex", "gemm_cfg_table_cpu", "CFG_COLUMNS", "NUM_CFG",
            "default_cfg", "check_device_errors", "GemmError", "reset_workspaces"]

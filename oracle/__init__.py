@@ -11,6 +11,8 @@ from .gemm_oracle import (  # noqa: F401
     build,
     f16_to_f32,
     f32_to_f16,
+    ACTIVATIONS,
+    gemm_ex,
     gemm_f16,
     gemm_f16_numpy,
     load,

@@ -25,6 +25,15 @@
  * Hence the result is independent of the reference's tile configuration and
  * this loop reproduces it bit for bit (pinned against the reference kernel
  * compiled from source, see oracle/ref_bank.cu and tests/golden/).
+ *
+ * oracle_gemm_ex extends the same accumulation past the reference, which
+ * only computed C = A*B on row-major operands: transposed storage of A or B
+ * (the element A[r][k] / B[k][c] is read from the transposed position, the
+ * sum is unchanged) and the library's fused epilogue, defined as
+ *   C = fp16_rne(act(alpha * acc + beta * D + bias[c]))
+ * in fp32, with beta * D added by fmaf and D not read when beta == 0.  That
+ * part has no reference counterpart to pin; it restates the definition the
+ * library documents (include/gemm_sm100.h, gemm_launch_ex).
  */
 #include <math.h>
 #include <pthread.h>
@@ -83,7 +92,23 @@ typedef struct {
   uint16_t* C;
   int64_t M, N, K, lda, ldb, ldc;
   int64_t r0, r1, c0, c1;
+  /* fused epilogue (epi != 0) */
+  int epi, act;
+  float alpha, beta;
+  const uint16_t* D;
+  int64_t ldd;
+  const uint16_t* bias;
 } oracle_job;
+
+/* act(alpha * acc + beta * D[r][c] + bias[c]) in fp32. */
+static float oracle_epilogue(const oracle_job* j, float acc, int64_t r, int64_t c) {
+  float v = j->alpha * acc;
+  if (j->beta != 0.0f) v = fmaf(j->beta, oracle_f16_to_f32(j->D[r * j->ldd + c]), v);
+  v += j->bias ? oracle_f16_to_f32(j->bias[c]) : 0.0f;
+  if (j->act == 1) return v > 0.0f ? v : 0.0f;
+  if (j->act == 2) return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+  return v;
+}
 
 #define ORACLE_KBLK 64
 
@@ -120,7 +145,11 @@ static void* oracle_worker(void* arg) {
   }
   for (int64_t r = 0; r < nr; ++r) {
     uint16_t* crow = j->C + (j->r0 + r) * j->ldc + j->c0;
-    for (int64_t c = 0; c < w; ++c) crow[c] = oracle_f32_to_f16(acc[r * w + c]);
+    if (j->epi) {
+      for (int64_t c = 0; c < w; ++c) crow[c] = oracle_f32_to_f16(oracle_epilogue(j, acc[r * w + c], j->r0 + r, j->c0 + c));
+    } else {
+      for (int64_t c = 0; c < w; ++c) crow[c] = oracle_f32_to_f16(acc[r * w + c]);
+    }
   }
   free(acc);
   free(bf);
@@ -132,10 +161,8 @@ static void* oracle_worker(void* arg) {
  * Work is split over `nthreads` POSIX threads by column slices (rows when N
  * is narrow).  Returns 0 on success.
  */
-int oracle_gemm_f16(const uint16_t* A, const uint16_t* B, uint16_t* C, int64_t M, int64_t N, int64_t K,
-                    int64_t lda, int64_t ldb, int64_t ldc, int nthreads) {
-  if (M < 0 || N < 0 || K < 0) return 1;
-  if (M == 0 || N == 0) return 0;
+static int oracle_run(const oracle_job* proto, int nthreads) {
+  const int64_t M = proto->M, N = proto->N;
   if (nthreads < 1) nthreads = 1;
   if (nthreads > 256) nthreads = 256;
   oracle_job jobs[256];
@@ -146,16 +173,7 @@ int oracle_gemm_f16(const uint16_t* A, const uint16_t* B, uint16_t* C, int64_t M
   const int by_cols = cblocks >= nthreads || cblocks >= M;
   int nj = 0;
   for (int t = 0; t < nthreads; ++t) {
-    oracle_job j;
-    j.A = A;
-    j.B = B;
-    j.C = C;
-    j.M = M;
-    j.N = N;
-    j.K = K;
-    j.lda = lda;
-    j.ldb = ldb;
-    j.ldc = ldc;
+    oracle_job j = *proto;
     if (by_cols) {
       const int64_t b0 = cblocks * t / nthreads, b1 = cblocks * (t + 1) / nthreads;
       j.r0 = 0;
@@ -182,5 +200,86 @@ int oracle_gemm_f16(const uint16_t* A, const uint16_t* B, uint16_t* C, int64_t M
       if (ret != NULL) rc = 2;
     }
   }
+  return rc;
+}
+
+int oracle_gemm_f16(const uint16_t* A, const uint16_t* B, uint16_t* C, int64_t M, int64_t N, int64_t K,
+                    int64_t lda, int64_t ldb, int64_t ldc, int nthreads) {
+  if (M < 0 || N < 0 || K < 0) return 1;
+  if (M == 0 || N == 0) return 0;
+  oracle_job j;
+  memset(&j, 0, sizeof(j));
+  j.A = A;
+  j.B = B;
+  j.C = C;
+  j.M = M;
+  j.N = N;
+  j.K = K;
+  j.lda = lda;
+  j.ldb = ldb;
+  j.ldc = ldc;
+  return oracle_run(&j, nthreads);
+}
+
+/* Row-major copy (rows x cols, pitch cols) of the transpose of a cols x rows
+ * matrix stored with pitch ld. */
+static uint16_t* oracle_transpose(const uint16_t* src, int64_t ld, int64_t rows, int64_t cols) {
+  uint16_t* dst = (uint16_t*)malloc((size_t)(rows * cols > 0 ? rows * cols : 1) * sizeof(uint16_t));
+  if (!dst) return NULL;
+  for (int64_t c = 0; c < cols; ++c)
+    for (int64_t r = 0; r < rows; ++r) dst[r * cols + c] = src[c * ld + r];
+  return dst;
+}
+
+/*
+ * C = act(alpha * op(A) op(B) + beta * D + bias), op(A) = A (stored M x K,
+ * pitch lda) or A^T (trans_a: stored K x M), op(B) = B (stored K x N) or B^T
+ * (trans_b: stored N x K).  act: 0 none, 1 ReLU, 2 GELU (erf form).
+ * The accumulation is oracle_gemm_f16's, element for element.
+ */
+int oracle_gemm_ex(const uint16_t* A, const uint16_t* B, uint16_t* C, int64_t M, int64_t N, int64_t K,
+                   int64_t lda, int64_t ldb, int64_t ldc, int trans_a, int trans_b, float alpha, float beta,
+                   const uint16_t* D, int64_t ldd, const uint16_t* bias, int act, int nthreads) {
+  if (M < 0 || N < 0 || K < 0 || act < 0 || act > 2) return 1;
+  if (M == 0 || N == 0) return 0;
+  if (beta != 0.0f && (!D || ldd < N)) return 1;
+  uint16_t* At = NULL;
+  uint16_t* Bt = NULL;
+  if (trans_a && K > 0) {
+    At = oracle_transpose(A, lda, M, K);
+    if (!At) return 2;
+    A = At;
+    lda = K;
+  }
+  if (trans_b && K > 0) {
+    Bt = oracle_transpose(B, ldb, K, N);
+    if (!Bt) {
+      free(At);
+      return 2;
+    }
+    B = Bt;
+    ldb = N;
+  }
+  oracle_job j;
+  memset(&j, 0, sizeof(j));
+  j.A = A;
+  j.B = B;
+  j.C = C;
+  j.M = M;
+  j.N = N;
+  j.K = K;
+  j.lda = lda;
+  j.ldb = ldb;
+  j.ldc = ldc;
+  j.epi = (alpha != 1.0f || beta != 0.0f || bias != NULL || act != 0);
+  j.act = act;
+  j.alpha = alpha;
+  j.beta = beta;
+  j.D = D;
+  j.ldd = ldd;
+  j.bias = bias;
+  const int rc = oracle_run(&j, nthreads);
+  free(At);
+  free(Bt);
   return rc;
 }

@@ -8,6 +8,9 @@ Only tests/, ``__graft_entry__.smoke()`` and the CPU-baseline leg of
   accumulator updated in ascending k, rounded once to fp16 (RNE).
 * :func:`gemm_f16_numpy` -- the same loop written with numpy (vectorised over
   the output, sequential in k), an independent restatement for small cases.
+* :func:`gemm_ex` -- the same accumulation with transposed operand storage
+  and the library's fused epilogue (alpha, beta * D, bias, ReLU / GELU),
+  which has no reference counterpart (see gemm_oracle.c).
 * :func:`tolerance` -- the acceptance bound of the build's parity tests:
   |err| <= 1e-2 * sqrt(K/1024) * max|C_ref| + 1e-3.
 """
@@ -43,6 +46,10 @@ def load() -> ctypes.CDLL:
         lib = ctypes.CDLL(str(_LIB_PATH))
         lib.oracle_gemm_f16.restype = ctypes.c_int
         lib.oracle_gemm_f16.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int64] * 6 + [ctypes.c_int]
+        lib.oracle_gemm_ex.restype = ctypes.c_int
+        lib.oracle_gemm_ex.argtypes = ([ctypes.c_void_p] * 3 + [ctypes.c_int64] * 6 + [ctypes.c_int] * 2 +
+                                       [ctypes.c_float] * 2 + [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+                                                               ctypes.c_int, ctypes.c_int])
         lib.oracle_f32_to_f16.restype = ctypes.c_uint16
         lib.oracle_f32_to_f16.argtypes = [ctypes.c_float]
         lib.oracle_f16_to_f32.restype = ctypes.c_float
@@ -72,6 +79,45 @@ def gemm_f16(A: np.ndarray, B: np.ndarray, threads: Optional[int] = None) -> np.
     rc = load().oracle_gemm_f16(A.ctypes.data, B.ctypes.data, C.ctypes.data, M, N, K, K, N, N, _threads(threads))
     if rc != 0:
         raise RuntimeError(f"oracle_gemm_f16 failed ({rc})")
+    return C
+
+
+ACTIVATIONS = {"none": 0, "relu": 1, "gelu": 2}
+
+
+def gemm_ex(A: np.ndarray, B: np.ndarray, trans_a: bool = False, trans_b: bool = False, alpha: float = 1.0,
+            beta: float = 0.0, D: Optional[np.ndarray] = None, bias: Optional[np.ndarray] = None,
+            activation: str = "none", threads: Optional[int] = None) -> np.ndarray:
+    """act(alpha * op(A) @ op(B) + beta * D + bias) with the same accumulation as :func:`gemm_f16`.
+
+    A and B are given as stored: A is M x K (or K x M when ``trans_a``), B is
+    K x N (or N x K when ``trans_b``).  The epilogue is evaluated in fp32 and
+    rounded once to fp16; D is not read when beta == 0.
+    """
+    A = np.ascontiguousarray(A, dtype=np.float16)
+    B = np.ascontiguousarray(B, dtype=np.float16)
+    M, K = (A.shape[1], A.shape[0]) if trans_a else A.shape
+    Kb, N = (B.shape[1], B.shape[0]) if trans_b else B.shape
+    if K != Kb:
+        raise ValueError(f"bad shapes {A.shape} (trans {trans_a}) x {B.shape} (trans {trans_b})")
+    d_ptr, ldd = None, 0
+    if beta != 0.0:
+        D = np.ascontiguousarray(D, dtype=np.float16)
+        if D.shape != (M, N):
+            raise ValueError(f"D must be {(M, N)}")
+        d_ptr, ldd = D.ctypes.data, N
+    b_ptr = None
+    if bias is not None:
+        bias = np.ascontiguousarray(bias, dtype=np.float16).reshape(-1)
+        if bias.shape != (N,):
+            raise ValueError(f"bias must have {N} elements")
+        b_ptr = bias.ctypes.data
+    C = np.empty((M, N), dtype=np.float16)
+    rc = load().oracle_gemm_ex(A.ctypes.data, B.ctypes.data, C.ctypes.data, M, N, K, A.shape[1], B.shape[1], N,
+                               int(trans_a), int(trans_b), float(alpha), float(beta), d_ptr, ldd, b_ptr,
+                               ACTIVATIONS[activation], _threads(threads))
+    if rc != 0:
+        raise RuntimeError(f"oracle_gemm_ex failed ({rc})")
     return C
 
 
