@@ -270,6 +270,50 @@ __device__ __forceinline__ void apply_epilogue64(const GemmParams& p, float (&f)
   }
 }
 
+// Loads D[row0 .. row0+31][col0 .. col0+63] (one epilogue warp's box) with
+// coalesced 16-byte reads: in step i lane l reads row 4i + l/8, segment l%8,
+// so each instruction covers four whole 128-byte rows.  Out-of-range
+// elements read 0.  The box is handed to the owning threads through shared
+// memory (transpose_d_box).
+__device__ __forceinline__ void load_d_box(const GemmParams& p, int row0, int col0, int lane, uint4 (&draw)[8]) {
+  const int seg = lane & 7;
+  const int c = col0 + seg * 8;
+  const bool vec = ((reinterpret_cast<uintptr_t>(p.D) | static_cast<uintptr_t>(p.ldd * 2)) & 15u) == 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = row0 + 4 * i + (lane >> 3);
+    draw[i] = make_uint4(0u, 0u, 0u, 0u);
+    if (r >= p.M || c >= p.N) continue;
+    const __half* src = p.D + static_cast<long long>(r) * p.ldd + c;
+    if (vec && c + 8 <= p.N) {
+      draw[i] = __ldcg(reinterpret_cast<const uint4*>(src));
+    } else {
+      const unsigned short* s = reinterpret_cast<const unsigned short*>(src);
+      unsigned short h[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) h[e] = (c + e < p.N) ? s[e] : static_cast<unsigned short>(0);
+      draw[i] = make_uint4(h[0] | (static_cast<uint32_t>(h[1]) << 16), h[2] | (static_cast<uint32_t>(h[3]) << 16),
+                           h[4] | (static_cast<uint32_t>(h[5]) << 16), h[6] | (static_cast<uint32_t>(h[7]) << 16));
+    }
+  }
+}
+
+// Writes a box loaded by load_d_box into a [32 x 128 B] staging buffer (the
+// 128-byte swizzle of the C staging layout, conflict-free both ways) and
+// returns this lane's own row in dv.  The buffer must be free; the caller
+// overwrites only its own row afterwards, so no further sync is needed.
+__device__ __forceinline__ void transpose_d_box(uint8_t* buf, int lane, const uint4 (&draw)[8], uint4 (&dv)[8]) {
+  const int seg = lane & 7;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = 4 * i + (lane >> 3);
+    *reinterpret_cast<uint4*>(buf + r * 128 + ((seg ^ (r & 7)) << 4)) = draw[i];
+  }
+  __syncwarp();
+#pragma unroll
+  for (int q = 0; q < 8; ++q) dv[q] = *reinterpret_cast<const uint4*>(buf + lane * 128 + ((q ^ (lane & 7)) << 4));
+}
+
 // Reduction of a split tile by the 128 epilogue threads of the CTA that
 // brought its last K piece: C[row0 + r][col0 + c] = sum over parts (in K
 // order) of the fp32 partial slots, for the tile's valid rows/columns.  The
@@ -632,6 +676,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     Unit w;
     while (work_next(p, cluster_id, num_clusters, wi, w)) {
       const int tm = w.tm, tn = w.tn;
+      // D of the tile's first chunk is requested before the accumulator is
+      // ready, so its latency hides under the mainloop.
+      const bool use_d = p.epi && p.beta != 0.0f;
+      uint4 draw[8];
+      if (use_d) load_d_box(p, tm * (kBM * CG) + static_cast<int>(rank) * kBM + ew * 32, tn * BN, lane, draw);
       // All four warps take the same decision, so none is left waiting at a
       // later named barrier if another gave up.
       ok = named_bar_and(1, 32 * kEpiWarps, mbar_wait(&tfull_bar[acc], acc_phase, abort_flag));
@@ -696,16 +745,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 #pragma unroll 1
         for (int c64 = 0; c64 < BN / 64; ++c64) {
           const int col0 = tn * BN + c64 * 64;
-          // D for this row chunk: issued before the TMEM reads so that its
-          // latency overlaps them
-          uint4 dv[8];
-          if (p.epi && p.beta != 0.0f && row_ok && col0 < p.N) {
-            const __half* drow = p.D + static_cast<long long>(grow) * p.ldd + col0;
-            load_chunk64(drow, p.N - col0, (reinterpret_cast<uintptr_t>(drow) & 15u) == 0, dv);
-          } else {
-#pragma unroll
-            for (int q = 0; q < 8; ++q) dv[q] = make_uint4(0u, 0u, 0u, 0u);
-          }
+          const int row0 = cta_row0 + ew * 32;
+          // D of this chunk (the first was requested before the wait): issued
+          // before the TMEM reads so that its latency overlaps them
+          if (use_d && c64 > 0) load_d_box(p, row0, col0, lane, draw);
           float f[64];
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
@@ -742,14 +785,22 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 #pragma unroll
             for (int i = 0; i < 64; ++i) f[i] = s[i];
           }
-          if (p.epi && col0 < p.N) apply_epilogue64(p, f, dv, col0);
           uint8_t* buf = cbufs + cb * Plan::kCBufBytes;
           if (p.c_tma) {
             if (lane == 0) bulk_wait_group_read<1>();
             __syncwarp();
           }
+          if (p.epi && col0 < p.N) {
+            uint4 dv[8];
+            if (use_d) {
+              transpose_d_box(buf, lane, draw, dv);
+            } else {
+#pragma unroll
+              for (int q = 0; q < 8; ++q) dv[q] = make_uint4(0u, 0u, 0u, 0u);
+            }
+            apply_epilogue64(p, f, dv, col0);
+          }
           stage_row_sw128(buf, lane, f);
-          const int row0 = cta_row0 + ew * 32;
           if (p.c_tma) {
             fence_proxy_async_smem();
             __syncwarp();

@@ -101,6 +101,23 @@ def menu() -> Tuple[List[str], List[Tuple[int, ...]]]:
     return cols, rows
 
 
+_menu_cache: List[Tuple[int, ...]] = []
+_cols_cache: List[str] = []
+
+
+def menu_row(cfg_id: int) -> Tuple[int, ...]:
+    """Knob tuple of one menu entry (the menu is read once)."""
+    if not _menu_cache:
+        _menu_cache.extend(menu()[1])
+    return _menu_cache[cfg_id]
+
+
+def menu_columns() -> List[str]:
+    if not _cols_cache:
+        _cols_cache.extend(lib.gemm_cfg_col_name(i).decode() for i in range(lib.gemm_cfg_num_cols()))
+    return list(_cols_cache)
+
+
 def cfg_find(knobs) -> int:
     ncol = lib.gemm_cfg_num_cols()
     k = list(knobs)

@@ -12,7 +12,8 @@ peaks (2250 TFLOP/s dense fp16, 8000 GB/s) and the measured ones
 (MEASURED_PEAKS.json: bf16 GEMM burst, HBM copy) are reported.
 
     python -m infinite_dreams.bench_shapes [--sets single,square,skinny,irregular]
-                                           [--iters 20] [--out results/shapes.json]
+                                           [--layout nn|tn|nt|tt] [--epilogue none|bias_gelu|residual]
+                                           [--torch] [--iters 20] [--out results/shapes.json]
 """
 from __future__ import annotations
 
@@ -49,7 +50,41 @@ def _shapes_of(name: str):
     return shape_sets()[name]
 
 
-def run(sets: List[str], iters: int, warmup: int, cfg_override: Optional[int] = None) -> List[Dict[str, object]]:
+EPILOGUES = ("none", "bias_gelu", "residual")
+
+
+def _ops(case, layout: str, epilogue: str, cid: int, out):
+    """(this build's call, torch's call) for one shape, layout and epilogue.
+
+    layout: two letters for A and B, "n" = row-major as the reference stores
+    them, "t" = stored transposed (read in place through a transposed view).
+    epilogue: "none"; "bias_gelu" = gelu(A @ B + bias); "residual" =
+    A @ B + C with C updated in place.  torch's call is cuBLAS (+ its own
+    elementwise kernels), the same work on the same views.
+    """
+    import torch
+
+    from . import infinite_dreams_ext as ext
+
+    A = case.A.t().contiguous().t() if layout[0] == "t" else case.A
+    B = case.B.t().contiguous().t() if layout[1] == "t" else case.B
+    N = B.shape[1]
+    if epilogue == "none":
+        if layout == "nn":
+            return (lambda: ext.gemm_forward_cfg(A, B, cid, out=out)), (lambda: torch.matmul(A, B, out=out))
+        return (lambda: ext.gemm_ex(A, B, cfg_id=cid, out=out)), (lambda: torch.matmul(A, B, out=out))
+    if epilogue == "bias_gelu":
+        bias = torch.rand((N,), device=A.device, dtype=torch.float16) - 0.5
+        return ((lambda: ext.gemm_ex(A, B, bias=bias, activation="gelu", cfg_id=cid, out=out)),
+                (lambda: torch.nn.functional.gelu(torch.addmm(bias, A, B))))
+    if epilogue == "residual":
+        return ((lambda: ext.gemm_ex(A, B, beta=1.0, C=out, cfg_id=cid, out=out)),
+                (lambda: out.addmm_(A, B)))
+    raise ValueError(epilogue)
+
+
+def run(sets: List[str], iters: int, warmup: int, cfg_override: Optional[int] = None, layout: str = "nn",
+        epilogue: str = "none", with_torch: bool = False) -> List[Dict[str, object]]:
     import torch
 
     from . import dispatch, infinite_dreams_ext as ext
@@ -63,17 +98,18 @@ def run(sets: List[str], iters: int, warmup: int, cfg_override: Optional[int] = 
         for (M, N, K) in _shapes_of(name):
             (case,) = make_bench_cases([(M, N, K)], seed=0, dist="skinny" if name == "skinny" else "uniform")
             cid = cfg_override if cfg_override is not None else dispatch.lookup(M, N, K)
-            out = torch.empty((M, N), dtype=torch.float16, device="cuda")
-            ms = time_cuda_ms(lambda: ext.gemm_forward_cfg(case.A, case.B, cid, out=out), iters=iters,
-                              warmup=warmup, flush_l2=True)
+            out = torch.zeros((M, N), dtype=torch.float16, device="cuda")
+            ours, theirs = _ops(case, layout, epilogue, cid, out)
+            ms = time_cuda_ms(ours, iters=iters, warmup=warmup, flush_l2=True)
             # back-to-back launches on warm caches, the way the reference's
             # tuner timed its kernels (infinite_dreams/utils.py:13-27)
-            ms_warm = time_cuda_ms(lambda: ext.gemm_forward_cfg(case.A, case.B, cid, out=out), iters=iters,
-                                   warmup=warmup, flush_l2=False)
+            ms_warm = time_cuda_ms(ours, iters=iters, warmup=warmup, flush_l2=False)
+            ms_torch = time_cuda_ms(theirs, iters=iters, warmup=warmup, flush_l2=True) if with_torch else None
             flops = 2.0 * M * N * K
             nbytes = 2.0 * (M * K + K * N + M * N)
             rows.append({
-                "set": name, "M": M, "N": N, "K": K, "cfg_id": cid,
+                "set": name, "M": M, "N": N, "K": K, "layout": layout, "epilogue": epilogue, "cfg_id": cid,
+                "ms_torch_cublas": ms_torch,
                 "knobs": dict(zip(ext.CFG_COLUMNS, table[cid].tolist())), "ms": ms, "ms_warm_b2b": ms_warm,
                 "tflops": flops / (ms * 1e-3) / 1e12, "gbs": nbytes / (ms * 1e-3) / 1e9,
                 "pct_fp16_peak_nominal": 100.0 * flops / (ms * 1e-3) / 1e12 / NOMINAL_TFLOPS,
@@ -94,13 +130,19 @@ def main(argv: Optional[List[str]] = None) -> None:
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--cfg", type=int, default=None)
+    ap.add_argument("--layout", default="nn", choices=["nn", "tn", "nt", "tt"],
+                    help="storage of A and B: n = row-major, t = stored transposed (read in place)")
+    ap.add_argument("--epilogue", default="none", choices=EPILOGUES)
+    ap.add_argument("--torch", action="store_true", help="also time torch (cuBLAS) on the same views")
     ap.add_argument("--out", default="results/shapes.json")
     args = ap.parse_args(argv)
-    rows = run(args.sets.split(","), args.iters, args.warmup, args.cfg)
+    rows = run(args.sets.split(","), args.iters, args.warmup, args.cfg, args.layout, args.epilogue, args.torch)
     os.makedirs(os.path.dirname(args.out) or ".", exist_ok=True)
     Path(args.out).write_text(json.dumps(rows, indent=1) + "\n")
     for r in rows:
-        print(f"{r['set']:9s} {r['M']:6d} {r['N']:6d} {r['K']:6d}  {r['ms']:8.4f} ms (warm {r['ms_warm_b2b']:8.4f})  "
+        tq = f" torch {r['ms_torch_cublas']:8.4f}" if r["ms_torch_cublas"] is not None else ""
+        print(f"{r['set']:9s} {r['M']:6d} {r['N']:6d} {r['K']:6d} {r['layout']} {r['epilogue']:9s} "
+              f"{r['ms']:8.4f} ms (warm {r['ms_warm_b2b']:8.4f}){tq}  "
               f"{r['tflops']:7.1f} TF/s "
               f"{r['gbs']:7.0f} GB/s  {r['pct_roofline_nominal']:5.1f}% roof(nom) "
               f"{r['pct_roofline_measured']:5.1f}% roof(meas)  {r['bound']}  {tuple(r['knobs'].values())}")

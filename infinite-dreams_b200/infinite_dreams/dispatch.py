@@ -68,16 +68,42 @@ def save_entry(M: int, N: int, K: int, knobs: Sequence[int], ms: float, columns:
         _cache.pop(str(p), None)
 
 
-def lookup(M: int, N: int, K: int, path: Optional[os.PathLike] = None) -> int:
-    """cfg_id for a shape: the tuned entry if present and valid, else the heuristic."""
+EPILOGUE_SUFFIX = "+epi"
+
+
+def lookup(M: int, N: int, K: int, path: Optional[os.PathLike] = None, epilogue: bool = False) -> int:
+    """cfg_id for a shape: the tuned entry if present and valid, else the heuristic.
+
+    ``epilogue``: the launch has a fused epilogue that reads D or applies an
+    activation.  A tuned ``MxNxK+epi`` entry is used when present.  Otherwise
+    a 512-column pair tile (one TMEM accumulator, so the next tile's MMAs wait
+    for the whole epilogue) is replaced by the 256-column pair tile with the
+    same other knobs, whose two accumulators let the epilogue of one tile run
+    under the mainloop of the next.
+    """
     from . import _capi
 
-    entry = load_table(path).get(shape_key(M, N, K))
+    table = load_table(path)
+    cid = -1
+    if epilogue:
+        entry = table.get(shape_key(M, N, K) + EPILOGUE_SUFFIX)
+        if entry is not None and _capi.cfg_find(entry["knobs"]) >= 0:
+            return _capi.cfg_find(entry["knobs"])
+    entry = table.get(shape_key(M, N, K))
     if entry is not None:
         cid = _capi.cfg_find(entry["knobs"])
-        if cid >= 0:
-            return cid
-    return int(_capi.lib.gemm_default_cfg(int(M), int(N), int(K)))
+    if cid < 0:
+        cid = int(_capi.lib.gemm_default_cfg(int(M), int(N), int(K)))
+    if epilogue and cid >= 0:
+        cols = _capi.menu_columns()
+        row = _capi.menu_row(cid)
+        knobs = dict(zip(cols, row))
+        if knobs["tile_n"] == 512:
+            knobs["tile_n"] = 256
+            alt = _capi.cfg_find([knobs[c] for c in cols])
+            if alt >= 0:
+                return alt
+    return cid
 
 
 def gemm(A, B, out=None, path: Optional[os.PathLike] = None):
@@ -92,6 +118,8 @@ def gemm(A, B, out=None, path: Optional[os.PathLike] = None):
 def entries(path: Optional[os.PathLike] = None) -> Dict[Tuple[int, int, int], dict]:
     out = {}
     for k, v in load_table(path).items():
+        if k.endswith(EPILOGUE_SUFFIX):
+            continue
         m, n, kk = (int(x) for x in k.split("x"))
         out[(m, n, kk)] = v
     return out

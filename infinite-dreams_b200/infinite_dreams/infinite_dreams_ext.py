@@ -191,7 +191,7 @@ def gemm_ex(A: torch.Tensor, B: torch.Tensor, *, alpha: float = 1.0, beta: float
         bias = bias.reshape(N).contiguous()
     if cfg_id is None:
         from . import dispatch
-        cfg_id = dispatch.lookup(M, N, K)
+        cfg_id = dispatch.lookup(M, N, K, epilogue=(beta != 0.0 or activation != "none"))
     elif not 0 <= int(cfg_id) < NUM_CFG:
         raise RuntimeError("cfg_id out of range")
     with torch.cuda.device(dev):

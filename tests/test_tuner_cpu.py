@@ -137,3 +137,26 @@ def test_interleaved_confirmation_cancels_drift(menu):
     ranked, rows = tuner.rerank_topk(cands_rev, s, rounds=4)
     assert ranked[0][0].as_tuple() == (128, 192, 64, 4, 1, 1, 4, 3)   # interleaved: the true best
     assert len(rows) == 2
+
+
+def test_epilogue_lookup_prefers_double_buffered_pair_tile(tmp_path):
+    from infinite_dreams import _capi
+    path = tmp_path / "t.json"
+    wide = (256, 512, 64, 4, 2, 1, 8, 1)
+    dispatch.save_entry(8192, 8192, 8192, wide, 0.7, COLUMNS, path=path)
+    assert _capi.menu_row(dispatch.lookup(8192, 8192, 8192, path)) == wide
+    assert _capi.menu_row(dispatch.lookup(8192, 8192, 8192, path, epilogue=True)) == (256, 256, 64, 4, 2, 1, 8, 1)
+    # a tuned epilogue entry wins
+    own = (256, 256, 64, 5, 2, 0, 4, 1)
+    dispatch.save_entry(8192, 8192, 8192, own, 0.75, COLUMNS, path=path)
+    data = json.loads(path.read_text())
+    data["shapes"]["8192x8192x8192+epi"] = data["shapes"].pop("8192x8192x8192")
+    data["shapes"]["8192x8192x8192"] = {"knobs": list(wide), "ms": 0.7}
+    path.write_text(json.dumps(data))
+    dispatch._cache.clear()
+    assert _capi.menu_row(dispatch.lookup(8192, 8192, 8192, path, epilogue=True)) == own
+    assert (8192, 8192, 8192) in dispatch.entries(path) and len(dispatch.entries(path)) == 1
+    # without a table entry: the heuristic, narrowed the same way
+    big = dispatch.lookup(16384, 16384, 16384, tmp_path / "none.json")
+    narrowed = dispatch.lookup(16384, 16384, 16384, tmp_path / "none.json", epilogue=True)
+    assert _capi.menu_row(big)[1] == 512 and _capi.menu_row(narrowed)[1] == 256
