@@ -8,6 +8,9 @@ ABI) is compiled by nvcc in parallel and linked into one shared library at
 (static CUDA runtime, driver entry points looked up at run time), so it
 loads without torch.
 
+The torch binding (csrc/torch_ext.cpp -> infinite_dreams/_torch_ext*.so) is
+built after the library and links to it.
+
 Usage:  python infinite-dreams_b200/build.py [--jobs N] [--force] [--verbose-ptxas]
 """
 from __future__ import annotations
@@ -98,6 +101,49 @@ def build(jobs: int | None = None, force: bool = False, ptxas_v: bool = False, q
     return LIB
 
 
+def torch_ext_path() -> Path:
+    import sysconfig
+    return PKG_ROOT / "infinite_dreams" / ("_torch_ext" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_torch_ext(force: bool = False, quiet: bool = False) -> Path:
+    """Compiles csrc/torch_ext.cpp (the torch binding of the C ABI) against
+    the installed torch and links it to libgemm_sm100.so through $ORIGIN."""
+    import sysconfig
+
+    import torch
+    from torch.utils import cpp_extension as ce
+
+    src = CSRC / "torch_ext.cpp"
+    out = torch_ext_path()
+    key = hashlib.sha256(src.read_bytes() + (INCLUDE / "gemm_sm100.h").read_bytes() +
+                         torch.__version__.encode() + sysconfig.get_config_var("EXT_SUFFIX").encode()).hexdigest()
+    stamp = BUILD / "torch_ext.stamp"
+    if not force and out.exists() and stamp.exists() and stamp.read_text() == key:
+        if not quiet:
+            print(f"up to date: {out.name}")
+        return out
+    cuda_inc = str(Path(nvcc()).resolve().parent.parent / "include")
+    incs = ce.include_paths() + [cuda_inc, sysconfig.get_paths()["include"]]
+    libdirs = [str(Path(torch.__file__).parent / "lib")]
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    cmd = (["g++", "-O2", "-fPIC", "-shared", "-std=c++17", "-DTORCH_EXTENSION_NAME=_torch_ext",
+            "-DTORCH_API_INCLUDE_EXTENSION_H", f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-w"] +
+           [f"-I{d}" for d in incs] + [str(src), "-o", str(out) + ".tmp"] +
+           [f"-L{d}" for d in libdirs] + ["-lc10", "-ltorch", "-ltorch_cpu", "-ltorch_python", "-lc10_cuda",
+                                          "-ltorch_cuda", f"-L{LIB_DIR}", "-lgemm_sm100",
+                                          "-Wl,-rpath,$ORIGIN/_lib"])
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"torch extension build failed:\n{' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
+    os.replace(str(out) + ".tmp", out)
+    BUILD.mkdir(parents=True, exist_ok=True)
+    stamp.write_text(key)
+    if not quiet:
+        print(f"built: {out}")
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--jobs", type=int, default=None)
@@ -105,6 +151,7 @@ def main() -> None:
     ap.add_argument("--verbose-ptxas", action="store_true")
     args = ap.parse_args()
     build(args.jobs, args.force, args.verbose_ptxas)
+    build_torch_ext(args.force)
 
 
 if __name__ == "__main__":

@@ -26,6 +26,7 @@ and zero-initialised once, as the C ABI requires.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from typing import Dict, Optional, Tuple
 
@@ -36,6 +37,16 @@ from ._capi import GemmError, lib
 
 CFG_COLUMNS: Tuple[str, ...] = tuple(_capi.menu()[0])
 NUM_CFG: int = int(lib.gemm_num_cfgs())
+
+# The compiled torch binding of the same C ABI (csrc/torch_ext.cpp) takes the
+# per-call Python work off small launches; the ctypes path below remains for
+# builds without it (INFINITE_DREAMS_NO_TORCH_EXT=1 selects it explicitly).
+_fast = None
+if not os.environ.get("INFINITE_DREAMS_NO_TORCH_EXT"):
+    try:
+        from . import _torch_ext as _fast  # type: ignore[no-redef]
+    except ImportError:
+        _fast = None
 
 _ws_lock = threading.Lock()
 _workspaces: Dict[Tuple[int, int], torch.Tensor] = {}
@@ -60,6 +71,8 @@ def reset_workspaces() -> None:
     """Drops cached workspaces (needed after a device-side timeout)."""
     with _ws_lock:
         _workspaces.clear()
+    if _fast is not None:
+        _fast.reset_workspaces()
 
 
 def _check_inputs(A: torch.Tensor, B: torch.Tensor) -> None:
@@ -128,6 +141,8 @@ def gemm_forward(A: torch.Tensor, B: torch.Tensor, tile_m: int, tile_n: int, til
     if cfg_id < 0:
         raise RuntimeError(f"knob tuple {knobs} is not in the kernel bank menu "
                            f"(columns {', '.join(CFG_COLUMNS)})")
+    if _fast is not None:
+        return _fast.gemm_forward_cfg(A, B, cfg_id, out)
     return _launch(A, B, cfg_id, out)
 
 
@@ -138,6 +153,8 @@ def gemm_forward_cfg(A: torch.Tensor, B: torch.Tensor, cfg_id: int, *,
         raise RuntimeError("cfg_id must be >= 0")
     if cfg_id >= NUM_CFG:
         raise RuntimeError("cfg_id out of range")
+    if _fast is not None:
+        return _fast.gemm_forward_cfg(A, B, int(cfg_id), out)
     _check_inputs(A, B)
     return _launch(A, B, int(cfg_id), out)
 
@@ -178,6 +195,12 @@ def gemm_ex(A: torch.Tensor, B: torch.Tensor, *, alpha: float = 1.0, beta: float
     M, K = A.shape
     N = B.shape[1]
     dev = A.device
+    if _fast is not None:
+        if cfg_id is None:
+            from . import dispatch
+            cfg_id = dispatch.lookup(M, N, K, epilogue=(beta != 0.0 or activation != "none"))
+        return _fast.gemm_ex(A, B, int(cfg_id), float(alpha), float(beta), C, bias, _capi.ACTIVATIONS[activation],
+                             out)
     if beta != 0.0:
         if C is None:
             raise RuntimeError("beta != 0 needs C")

@@ -25,6 +25,7 @@ def _build_bank() -> None:
     spec.loader.exec_module(mod)
     jobs = int(os.environ.get("INFINITE_DREAMS_BUILD_JOBS", "0")) or None
     mod.build(jobs=jobs)
+    mod.build_torch_ext()
 
 
 class BuildBankExt(build_ext):
@@ -46,7 +47,7 @@ setup(
     description="sm_100a (B200) FP16 GEMM kernel bank with a C ABI, DE tuner and per-shape dispatch",
     packages=["infinite_dreams"],
     package_dir={"": "."},
-    package_data={"infinite_dreams": ["_lib/libgemm_sm100.so", "dispatch_table.json"]},
+    package_data={"infinite_dreams": ["_lib/libgemm_sm100.so", "_torch_ext*.so", "dispatch_table.json"]},
     python_requires=">=3.10",
     install_requires=["numpy", "torch"],
     cmdclass={"build_ext": BuildBankExt, "build_py": BuildPyWithBank},

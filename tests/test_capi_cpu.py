@@ -129,3 +129,17 @@ def test_reference_surface_names():
     with pytest.raises(RuntimeError, match="A must be CUDA tensor"):
         import torch
         ext.gemm_forward_cfg(torch.zeros(2, 2, dtype=torch.float16), torch.zeros(2, 2, dtype=torch.float16), 0)
+
+
+def test_torch_binding_loads_and_checks_on_cpu():
+    """The compiled torch binding of the C ABI loads and rejects non-CUDA inputs with the reference's message."""
+    import torch
+    from infinite_dreams import infinite_dreams_ext as ext
+    assert ext._fast is not None, "infinite_dreams/_torch_ext*.so missing: run build.py"
+    for name in ("gemm_forward_cfg", "gemm_ex", "reset_workspaces"):
+        assert hasattr(ext._fast, name)
+    A = torch.zeros((4, 4), dtype=torch.float16)
+    with pytest.raises(RuntimeError, match="A must be CUDA tensor"):
+        ext._fast.gemm_forward_cfg(A, A, 0)
+    with pytest.raises(RuntimeError, match="A must be CUDA tensor"):
+        ext._fast.gemm_ex(A, A, 0)

@@ -75,3 +75,28 @@ def test_bench_contract_small(cuda_device):
     assert d["value"] > 50 and np.isfinite(d["roofline"]["frac"])
     assert d["e2e"]["h2d_bytes_per_step"] == 2 * (2048 * 2048 * 2) and d["e2e"]["d2h_bytes_per_step"] == 2048 * 2048 * 2
     assert d["config"]["workload"].startswith("gemm 2048x2048x2048")
+
+
+def test_torch_binding_matches_ctypes_path(cuda_device):
+    """The compiled binding and the ctypes path launch the same kernels: identical bits."""
+    import torch
+    from infinite_dreams import infinite_dreams_ext as ext
+    assert ext._fast is not None
+    from helpers import make_inputs
+    for (M, N, K) in [(300, 700, 333), (64, 4096, 4096), (1024, 1024, 1024)]:
+        A, B = make_inputs(M, N, K, seed=M)
+        Ad, Bd = A.cuda(), B.cuda()
+        cid = ext.default_cfg(M, N, K)
+        fast = ext.gemm_forward_cfg(Ad, Bd, cid)
+        slow = ext._launch(Ad, Bd, cid, None)
+        assert torch.equal(fast.view(torch.int16), slow.view(torch.int16)), (M, N, K)
+        bias = torch.rand((N,), device="cuda").half()
+        W = Bd.t().contiguous()
+        y_fast = ext._fast.gemm_ex(Ad, W.t(), cid, 0.5, 0.0, None, bias, 2, None)
+        ext_fast, ext._fast = ext._fast, None
+        try:
+            y_slow = ext.gemm_ex(Ad, W.t(), bias=bias, activation="gelu", alpha=0.5, cfg_id=cid)
+        finally:
+            ext._fast = ext_fast
+        assert torch.equal(y_fast.view(torch.int16), y_slow.view(torch.int16)), (M, N, K)
+    ext.check_device_errors()
