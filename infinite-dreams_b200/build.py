@@ -46,7 +46,7 @@ def nvcc() -> str:
 
 
 def sources() -> List[Path]:
-    return [CSRC / "gemm_capi.cu", CSRC / "gemm_noalloc.cu"] + sorted(GEN.glob("gemm_bank_bn*.cu"))
+    return [CSRC / "gemm_capi.cu", CSRC / "gemm_noalloc.cu"] + sorted(GEN.glob("gemm_bank_*.cu"))
 
 
 def headers_digest() -> str:

@@ -18,6 +18,7 @@
 
 #include "../../include/gemm_sm100.h"
 #include "gemm_bank_common.cuh"
+#include "gemm_skinny_kernel.cuh"
 #include "generated/gemm_cfg_menu.inc"
 
 namespace idb {
@@ -39,6 +40,24 @@ static const Variant kVariants[] = {
 #define IDB_VARIANT(BN, ST, CG) {BN, ST, CG, &launch_bn##BN##_s##ST##_cg##CG},
 #include "generated/gemm_variants.inc"
 #undef IDB_VARIANT
+};
+
+#define IDB_SKINNY(TM, ST)                                                                               \
+  cudaError_t launch_skinny_tm##TM##_s##ST(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, \
+                                           int grid, int cluster, cudaStream_t stream);
+#include "generated/gemm_skinny_variants.inc"
+#undef IDB_SKINNY
+
+struct SkinnyVariant {
+  int tm;
+  int stages;
+  SkinnyLaunchFn fn;
+};
+
+static const SkinnyVariant kSkinnyVariants[] = {
+#define IDB_SKINNY(TM, ST) {TM, ST, &launch_skinny_tm##TM##_s##ST},
+#include "generated/gemm_skinny_variants.inc"
+#undef IDB_SKINNY
 };
 
 // Copies a row-major fp16 matrix into a buffer whose row pitch is a multiple
@@ -154,6 +173,7 @@ bool tma_addressable(const void* p, int64_t pitch_elems) {
 int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 
 struct Plan {
+  bool skinny = false;  // tile_m < 128: gemm_skinny_f16, split_k = CTAs per cluster
   int tile_m = 0, tile_n = 0, stages = 0, cg = 1, raster = 0, group = 1, split_k = 1;
   int tiles_m = 0, tiles_n = 0, num_tiles = 0, kb_total = 0;
   bool streamk = false;
@@ -193,6 +213,27 @@ int make_plan(const void* A, const void* B, int64_t M, int64_t N, int64_t K, int
     return fail(GEMM_ERR_UNSUPPORTED, "M, N, K must each be < 2^31");
   }
   const int* row = kMenu[cfg_id];
+  if (row[kColTileM] < kBM) {
+    // Skinny kernel: one cluster of split_k CTAs per (tile_m x 128) block of
+    // C; the K blocks are divided among the cluster.  A cluster size above
+    // the number of K blocks is lowered to the largest power of two that
+    // still gives every CTA work (same GEMM).
+    pl->skinny = true;
+    pl->tile_m = row[kColTileM];
+    pl->tile_n = kSkinnyN;
+    pl->stages = row[kColStages];
+    pl->tiles_m = static_cast<int>((M + pl->tile_m - 1) / pl->tile_m);
+    pl->tiles_n = static_cast<int>((N + kSkinnyN - 1) / kSkinnyN);
+    const int64_t blocks = static_cast<int64_t>(pl->tiles_m) * pl->tiles_n;
+    pl->kb_total = static_cast<int>((K + kBK - 1) / kBK);
+    int s = row[kColSplitK];
+    while (s > 1 && s > pl->kb_total) s /= 2;
+    pl->split_k = s;
+    if (blocks * s > (1ll << 31) - 1) return fail(GEMM_ERR_UNSUPPORTED, "too many output tiles");
+    pl->num_tiles = static_cast<int>(blocks);
+    pl->workers = static_cast<int>(blocks);
+    pl->max_parts = 1;
+  } else {
   pl->tile_m = row[kColTileM];
   pl->tile_n = row[kColTileN];
   pl->cg = row[kColMmaSm];
@@ -229,6 +270,7 @@ int make_plan(const void* A, const void* B, int64_t M, int64_t N, int64_t K, int
   }
   if (pl->max_parts > 1 && pl->num_tiles > kCounterSlots) {
     return fail(GEMM_ERR_UNSUPPORTED, "split-K / stream-K support at most 65536 output tiles");
+  }
   }
   pl->pack_a = M > 0 && K > 0 && !tma_addressable(A, lda);
   pl->pack_b = N > 0 && K > 0 && !tma_addressable(B, ldb);
@@ -406,10 +448,21 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
     return fail(GEMM_ERR_WORKSPACE, "workspace must be 256-byte aligned");
   }
   const Variant* var = nullptr;
-  for (const Variant& v : kVariants) {
-    if (v.bn == pl.tile_n && v.stages == pl.stages && v.cg == pl.cg) var = &v;
+  const SkinnyVariant* svar = nullptr;
+  if (pl.skinny) {
+    if (op.trans_a) {
+      return fail(GEMM_ERR_UNSUPPORTED, "skinny configurations (tile_m < 128) read A stored M x K (trans_a = 0)");
+    }
+    for (const SkinnyVariant& v : kSkinnyVariants) {
+      if (v.tm == pl.tile_m && v.stages == pl.stages) svar = &v;
+    }
+    if (!svar) return fail(GEMM_ERR_BAD_CFG, "no compiled skinny kernel for this configuration");
+  } else {
+    for (const Variant& v : kVariants) {
+      if (v.bn == pl.tile_n && v.stages == pl.stages && v.cg == pl.cg) var = &v;
+    }
+    if (!var) return fail(GEMM_ERR_BAD_CFG, "no compiled kernel for this configuration");
   }
-  if (!var) return fail(GEMM_ERR_BAD_CFG, "no compiled kernel for this configuration");
 
   uint8_t* wsb = static_cast<uint8_t*>(ws);
   const void* a_src = A;
@@ -431,6 +484,38 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
 
   CUtensorMap tmA, tmB, tmC;
   std::memset(&tmC, 0, sizeof(tmC));
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaGetDevice");
+  std::call_once(g_err_once[dev], [dev] {
+    g_err_status[dev] = cudaGetSymbolAddress(reinterpret_cast<void**>(&g_err_word[dev]), g_device_error);
+  });
+  if (g_err_status[dev] != cudaSuccess) return fail_cuda(g_err_status[dev], "cudaGetSymbolAddress(g_device_error)");
+  p.err = g_err_word[dev];
+
+  if (pl.skinny) {
+    // A: [tile_m rows x 64 K] boxes; B: [128 n x 64 K] (stored N x K) or
+    // [64 K x 64 n] atoms (stored K x N); C is written with plain stores.
+    st = encode_2d_cached(&tmA, a_src, K, M, a_ld, kBK, pl.tile_m, "A");
+    if (st != GEMM_OK) return st;
+    if (op.trans_b) {
+      st = encode_2d_cached(&tmB, b_src, K, N, b_ld, kBK, kSkinnyN, "B (stored N x K)");
+    } else {
+      st = encode_2d_cached(&tmB, b_src, N, K, b_ld, 64, kBK, "B");
+    }
+    if (st != GEMM_OK) return st;
+    p.kb_total = pl.kb_total;
+    p.tiles_m = pl.tiles_m;
+    p.tiles_n = pl.tiles_n;
+    p.num_tiles = pl.num_tiles;
+    p.split_k = pl.split_k;
+    p.partials = nullptr;
+    p.counters = nullptr;
+    e = svar->fn(tmA, tmB, p, pl.num_tiles * pl.split_k, pl.split_k, stream);
+    if (e != cudaSuccess) return fail_cuda(e, "skinny gemm kernel launch");
+    return GEMM_OK;
+  }
+
   // Boxes: K-major A [64 K x 128 rows]; M-major A, and B either way, in
   // 64 x 64 atoms (see the producer in gemm_sm100_kernel.cuh).
   if (op.trans_a) {
@@ -451,15 +536,6 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
     if (st != GEMM_OK) return st;
   }
 
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return fail_cuda(e, "cudaGetDevice");
-  std::call_once(g_err_once[dev], [dev] {
-    g_err_status[dev] = cudaGetSymbolAddress(reinterpret_cast<void**>(&g_err_word[dev]), g_device_error);
-  });
-  if (g_err_status[dev] != cudaSuccess) return fail_cuda(g_err_status[dev], "cudaGetSymbolAddress(g_device_error)");
-  int* err_word = g_err_word[dev];
-
   p.tiles_m = pl.tiles_m;
   p.tiles_n = pl.tiles_n;
   p.num_tiles = pl.num_tiles;
@@ -473,7 +549,6 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
   p.c_tma = c_tma ? 1 : 0;
   p.partials = pl.max_parts > 1 ? reinterpret_cast<float*>(wsb + pl.off_partials) : nullptr;
   p.counters = pl.max_parts > 1 ? reinterpret_cast<unsigned int*>(wsb) : nullptr;
-  p.err = err_word;
 
   // persistent grid: one CTA (or CTA pair) per SM (pair), at most one per work unit
   const int grid = pl.workers * pl.cg;
@@ -595,6 +670,20 @@ int gemm_default_cfg(int64_t M, int64_t N, int64_t K) {
   //    occupy the 148 SMs.
   const int kSms = 148;
   const int64_t pairs = kSms / 2;
+  const int64_t kb = (K + kBK - 1) / kBK;
+  if (M >= 1 && M <= 64) {
+    // Few rows: the skinny kernel (C^T tiles of 128 columns, split-K inside a
+    // cluster).  The smallest row tile that holds M, the deepest ring that
+    // fits, and the largest cluster that keeps about one wave with >= 4 K
+    // blocks per CTA.
+    const int tm = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
+    const int stages = tm == 16 ? 12 : (tm == 32 ? 10 : 8);
+    const int64_t blocks = (N + kSkinnyN - 1) / kSkinnyN;
+    int s = 1;
+    while (s < 8 && blocks * 2 * s <= kSms && kb / (2 * s) >= 4) s *= 2;
+    int knobs[IDB_MENU_COLS] = {tm, kSkinnyN, kBK, stages, 1, 0, 1, s};
+    return gemm_cfg_find(knobs, IDB_MENU_COLS);
+  }
   // Fraction of the last persistent wave's slots that have work.
   auto wave_fill = [pairs](int64_t tiles) {
     const int64_t waves = (tiles + pairs - 1) / pairs;
@@ -620,7 +709,6 @@ int gemm_default_cfg(int64_t M, int64_t N, int64_t K) {
     stages = 6;
   }
   const int64_t tiles = tm * ((N + tile_n - 1) / tile_n);
-  const int64_t kb = (K + kBK - 1) / kBK;
   int split = 1;
   if (tiles < kSms / 2 && kb >= 8) {
     const int choices[] = {16, 12, 8, 6, 4, 3, 2};

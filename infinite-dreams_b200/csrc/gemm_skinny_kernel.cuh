@@ -1,0 +1,304 @@
+// Skinny FP16 GEMM (few rows of A) for sm_100a:  C[M,N] = A[M,K] * B[K,N].
+//
+// Same arithmetic as the reference kernel (src/gemm_kernels.cuh:6-83): fp16
+// operands, fp32 accumulation, one rounding to fp16 (plus the optional fused
+// epilogue of gemm_launch_ex).  Built for M <= 64, where a 128-row MMA tile
+// would be mostly zero fill and the cost is streaming B from HBM:
+//
+//  * operands swapped: the MMA computes C^T = B^T A^T, so 128 columns of C
+//    fill the 128 TMEM lanes (MMA M = 128) and the few rows of A are the MMA
+//    N (TM = 16, 32 or 64).  Per pipeline stage a CTA loads a [64 K x 128 n]
+//    tile of B (16 KiB, all useful) and a [TM x 64 K] tile of A (2-8 KiB), so
+//    the ring holds 8-12 stages of B in flight;
+//  * split-K inside a thread-block cluster: the S CTAs of a cluster own the
+//    same 128 columns and S consecutive K ranges.  Each writes its fp32
+//    partial tile into its own (now idle) pipeline buffers; after a cluster
+//    barrier, CTA r sums columns [r*128/S, (r+1)*128/S) of all S partials
+//    through distributed shared memory, in rank order (deterministic), and
+//    stores C.  No workspace, no atomics, no second pass over global memory.
+//
+// Roles as in gemm_sm100_kernel.cuh: warp 0 TMA producer, warp 1 TMEM owner
+// and MMA issuer, warps 2..5 read the accumulator.  Every mbarrier wait is
+// bounded; both cluster barriers are reached by every thread on every path.
+#pragma once
+#include <atomic>
+#include <cuda_runtime.h>
+
+#include "gemm_sm100_kernel.cuh"
+
+namespace idb {
+
+constexpr int kSkinnyN = 128;  // columns of C per cluster: the 128 TMEM lanes
+
+template <int TM, int STAGES>
+struct SkinnyPlan {
+  static constexpr int kNBytes = kBK * kSkinnyN * 2;  // B tile: 16 KiB
+  static constexpr int kMBytes = TM * kBK * 2;        // A tile: TM rows of 128 B
+  static constexpr int kStageBytes = kNBytes + kMBytes;
+  static constexpr int kOffN = 0;
+  static constexpr int kOffM = STAGES * kNBytes;
+  static constexpr int kOffBar = kOffM + STAGES * kMBytes;
+  static constexpr int kNumBars = 2 * STAGES + 1;  // full, empty, tmem_full
+  static constexpr int kOffMisc = kOffBar + kNumBars * 8;
+  static constexpr int kUsed = kOffMisc + 16;
+  static constexpr int kDynamicBytes = kUsed + 1024;
+  static constexpr uint32_t kTmemCols = TM <= 32 ? 32 : 64;
+  static constexpr int kPartialBytes = TM * kSkinnyN * 4;  // fp32 [TM][128]
+  static_assert(TM == 16 || TM == 32 || TM == 64, "MMA N of the swapped tile");
+  static_assert(kMBytes % 1024 == 0, "swizzled A tiles need 1024-byte alignment");
+  static_assert(kPartialBytes <= kOffBar, "the partial tile reuses the pipeline buffers");
+};
+
+template <int TM, int STAGES>
+__global__ void __launch_bounds__(kNumThreads, 1)
+    gemm_skinny_f16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const GemmParams p) {
+  using Plan = SkinnyPlan<TM, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sN = smem + Plan::kOffN;
+  uint8_t* sM = smem + Plan::kOffM;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + Plan::kOffBar);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Plan::kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* partial = reinterpret_cast<float*>(smem);  // after the mainloop: fp32 [TM][128]
+
+  const int warp = static_cast<int>(threadIdx.x >> 5);
+  const int lane = static_cast<int>(threadIdx.x & 31);
+  const int S = static_cast<int>(cluster_nctarank());
+  const int rank = static_cast<int>(cluster_ctarank());
+  const int cid = static_cast<int>(cluster_id_x());
+  const int n0 = (cid % p.tiles_n) * kSkinnyN;
+  const int m0 = (cid / p.tiles_n) * TM;
+  const int kb0 = static_cast<int>(static_cast<long long>(rank) * p.kb_total / S);
+  const int kb1 = static_cast<int>(static_cast<long long>(rank + 1) * p.kb_total / S);
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(tfull_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc<1>(tmem_slot, Plan::kTmemCols);
+    tmem_relinquish<1>();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (issued >= STAGES && !mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        const int k0 = kb * kBK;
+        uint8_t* n_dst = sN + stage * Plan::kNBytes;
+        mbar_arrive_expect_tx(&full_bar[stage], Plan::kStageBytes);
+        if (p.b_kmaj) {
+          // B stored N x K: one [128 n x 64 K] box, K-major rows
+          tma_load_2d(n_dst, &tmB, &full_bar[stage], k0, n0);
+        } else {
+          // B stored K x N: two [64 K x 64 n] atoms, n-major
+          tma_load_2d(n_dst, &tmB, &full_bar[stage], n0, k0);
+          tma_load_2d(n_dst + kBK * 128, &tmB, &full_bar[stage], n0 + 64, k0);
+        }
+        tma_load_2d(sM + stage * Plan::kMBytes, &tmA, &full_bar[stage], k0, m0);
+        ++issued;
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicOr(p.err, kDevErrTimeoutProducer);
+      }
+      // the last min(issued, STAGES) fills must land before their buffers are reused
+      const int outstanding = issued < STAGES ? issued : STAGES;
+      for (int i = 0; i < outstanding; ++i) {
+        stage = (stage == 0) ? STAGES - 1 : stage - 1;
+        if (stage == STAGES - 1) phase ^= 1u;
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&full_bar[stage], phase)) {
+          if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            atomicOr(p.err, kDevErrTimeoutTeardown);
+            break;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      // A operand = the B tile (128 n rows), B operand = the A tile (TM rows, K-major)
+      const uint32_t idesc = idesc_f16_f32(kSkinnyN, TM, p.b_kmaj == 0, false);
+      const uint32_t n_lbo = p.b_kmaj ? 16 : kBK * 128, n_kstep = p.b_kmaj ? kUmmaK * 2 : kUmmaK * 128;
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&full_bar[stage], phase, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t nb = smem_u32(sN + stage * Plan::kNBytes);
+        const uint32_t mb = smem_u32(sM + stage * Plan::kMBytes);
+#pragma unroll
+        for (int j = 0; j < kBK / kUmmaK; ++j) {
+          mma_f16_ss<1>(tmem_base, smem_desc_sw128(nb + j * n_kstep, n_lbo, 1024),
+                        smem_desc_sw128(mb + j * (kUmmaK * 2), 16, 1024), idesc, (kb > kb0 || j > 0) ? 1u : 0u);
+        }
+        mma_commit<1>(&empty_bar[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        atomicOr(p.err, kDevErrTimeoutMma);
+      }
+      // tfull completes when every MMA above has retired (also what makes
+      // the pipeline buffers free for the partial tile and TMEM safe to free)
+      mma_commit<1>(tfull_bar);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(tfull_bar, 0)) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          atomicOr(p.err, kDevErrTimeoutTeardown);
+          break;
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ accumulator -> partial tile
+    const int ew = warp & 3;
+    const int n_local = ew * 32 + lane;
+    const bool ok = named_bar_and(1, 32 * kEpiWarps, mbar_wait(tfull_bar, 0, abort_flag));
+    tc_fence_after();
+    if (ok) {
+#pragma unroll
+      for (int c32 = 0; c32 < (TM + 31) / 32; ++c32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + c32 * 32, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if (c32 * 32 + i < TM) partial[(c32 * 32 + i) * kSkinnyN + n_local] = __uint_as_float(v[i]);
+        }
+      }
+    } else {
+      *abort_flag = 1;
+      atomicOr(p.err, kDevErrTimeoutEpilogue);
+    }
+  }
+
+  // ------------------------------------------------------------ cluster reduction
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync();  // every CTA's partial tile is written and visible in the cluster
+  {
+    const int ns = kSkinnyN / S;       // columns this CTA reduces
+    const int g_per_row = ns / 4;      // 4-column groups per row
+    const int groups = TM * g_per_row;
+    const uint32_t base = smem_u32(partial);
+    const bool vec = ((reinterpret_cast<uintptr_t>(p.C) | static_cast<uintptr_t>(p.ldc * 2)) & 7u) == 0;
+    for (int g = static_cast<int>(threadIdx.x); g < groups; g += kNumThreads) {
+      const int m = g / g_per_row;
+      const int n = rank * ns + (g - m * g_per_row) * 4;
+      const int gm = m0 + m, gn = n0 + n;
+      if (gm >= p.M || gn >= p.N) continue;
+      const uint32_t off = static_cast<uint32_t>((m * kSkinnyN + n) * 4);
+      float4 acc = ld_dsmem_f4(mapa_shared(base + off, 0));
+      for (int q = 1; q < S; ++q) {
+        const float4 x = ld_dsmem_f4(mapa_shared(base + off, static_cast<uint32_t>(q)));
+        acc.x += x.x;
+        acc.y += x.y;
+        acc.z += x.z;
+        acc.w += x.w;
+      }
+      float* v = &acc.x;
+      if (p.epi) {
+        for (int c = 0; c < 4 && gn + c < p.N; ++c) {
+          const float d = (p.beta != 0.0f) ? __half2float(p.D[static_cast<long long>(gm) * p.ldd + gn + c]) : 0.0f;
+          const float b = (p.bias != nullptr) ? __half2float(p.bias[gn + c]) : 0.0f;
+          v[c] = epilogue_value(p, v[c], d, b);
+        }
+      }
+      __half* dst = p.C + static_cast<long long>(gm) * p.ldc + gn;
+      if (vec && gn + 3 < p.N) {
+        uint2 hv;
+        hv.x = pack_half2(v[0], v[1]);
+        hv.y = pack_half2(v[2], v[3]);
+        *reinterpret_cast<uint2*>(dst) = hv;
+      } else {
+        for (int c = 0; c < 4 && gn + c < p.N; ++c) dst[c] = __float2half_rn(v[c]);
+      }
+    }
+  }
+  cluster_sync();  // no CTA leaves while a peer may still read its partial tile
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc<1>(tmem_base, Plan::kTmemCols);
+  }
+}
+
+template <int TM, int STAGES>
+cudaError_t launch_skinny(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, int grid, int cluster,
+                          cudaStream_t stream) {
+  using Plan = SkinnyPlan<TM, STAGES>;
+  auto kernel = gemm_skinny_f16<TM, STAGES>;
+  static std::atomic<unsigned long long> configured{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(configured.load(std::memory_order_acquire) & bit)) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Plan::kDynamicBytes);
+    if (e != cudaSuccess) return e;
+    configured.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(kNumThreads, 1, 1);
+  cfg.dynamicSmemBytes = Plan::kDynamicBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(cluster);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, a, b, p);
+}
+
+using SkinnyLaunchFn = cudaError_t (*)(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, int grid,
+                                       int cluster, cudaStream_t stream);
+
+}  // namespace idb
+
+#define IDB_DEFINE_SKINNY(TM, ST)                                                                         \
+  cudaError_t launch_skinny_tm##TM##_s##ST(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, \
+                                           int grid, int cluster, cudaStream_t stream) {                   \
+    return launch_skinny<TM, ST>(a, b, p, grid, cluster, stream);                                         \
+  }

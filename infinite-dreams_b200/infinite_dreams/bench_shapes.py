@@ -97,7 +97,12 @@ def run(sets: List[str], iters: int, warmup: int, cfg_override: Optional[int] = 
     for name in sets:
         for (M, N, K) in _shapes_of(name):
             (case,) = make_bench_cases([(M, N, K)], seed=0, dist="skinny" if name == "skinny" else "uniform")
-            cid = cfg_override if cfg_override is not None else dispatch.lookup(M, N, K)
+            if cfg_override is None:
+                cid = dispatch.lookup(M, N, K)
+            elif cfg_override < 0:
+                cid = ext.default_cfg(M, N, K)      # the C ABI's heuristic, ignoring tuned entries
+            else:
+                cid = cfg_override
             out = torch.zeros((M, N), dtype=torch.float16, device="cuda")
             ours, theirs = _ops(case, layout, epilogue, cid, out)
             ms = time_cuda_ms(ours, iters=iters, warmup=warmup, flush_l2=True)
@@ -129,7 +134,8 @@ def main(argv: Optional[List[str]] = None) -> None:
                     help="comma-separated shape sets (single, square, skinny, irregular, default, large) or MxNxK")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--cfg", type=int, default=None)
+    ap.add_argument("--cfg", type=int, default=None,
+                    help="menu id for every shape; -1 = the C ABI's heuristic (default: the dispatch table)")
     ap.add_argument("--layout", default="nn", choices=["nn", "tn", "nt", "tt"],
                     help="storage of A and B: n = row-major, t = stored transposed (read in place)")
     ap.add_argument("--epilogue", default="none", choices=EPILOGUES)

@@ -7,7 +7,11 @@ with a bucket round-robin and wrote one ``TRY_CFG`` chain per bank file.  On
 Blackwell the knobs that matter are different, so the space is redefined:
 
 ===========  ==========================================================
-tile_m       tile rows: 128 * mma_sm (one tcgen05 MMA of M = tile_m)
+tile_m       tile rows: 128 * mma_sm (one tcgen05 MMA of M = tile_m); or
+             16 / 32 / 64 for the skinny kernel (few rows of A: the MMA
+             computes C^T with 128 columns of C as its M and tile_m as its
+             N; tile_n = 128, split_k = K slices reduced inside a cluster of
+             1, 2, 4 or 8 CTAs through distributed shared memory)
 tile_n       tile columns: one MMA N <= 256, or 512 for a CTA pair (two MMAs
              per K step, one accumulator); each CTA holds tile_n / mma_sm
              columns of B, a multiple of 64 (one 128-byte swizzle atom)
@@ -34,6 +38,8 @@ Outputs (deterministic, committed under ``csrc/generated``):
 * ``gemm_variants.inc``      -- one ``IDB_VARIANT(BN, STAGES, CG)`` per instantiation
 * ``gemm_bank_bn<BN>_sm<S>.cu`` -- explicit instantiations, one file per
                                 (tile_n, mma_sm), so the bank compiles in parallel.
+* ``gemm_skinny_variants.inc`` / ``gemm_bank_skinny.cu`` -- the same for the
+                                skinny kernel's (tile_m, stages) pairs.
 """
 from __future__ import annotations
 
@@ -47,16 +53,23 @@ SMEM_CAP = 232448          # opt-in dynamic shared memory per CTA on sm_100 (227
 TMEM_COLS = 512            # TMEM columns per SM
 BM_PER_SM = 128            # rows one tcgen05 M=128 MMA covers
 
-TILE_MS = (128, 256)
+TILE_MS = (16, 32, 64, 128, 256)
 TILE_NS = (64, 128, 192, 256, 512)
 TILE_KS = (64,)
-STAGES = (2, 3, 4, 5, 6, 7, 8)
+STAGES = (2, 3, 4, 5, 6, 7, 8, 10, 12)
 MMA_SMS = (1, 2)
 RASTERS = (0, 1)
 GROUPS = (1, 2, 4, 8, 16)
 SPLIT_KS = (0, 1, 2, 3, 4, 6, 8, 12, 16)
 
 COLUMNS = ("tile_m", "tile_n", "tile_k", "stages", "mma_sm", "raster", "group", "split_k")
+
+# Skinny kernel (gemm_skinny_kernel.cuh): tile_m rows of A per cluster, 128
+# columns of C, K split over the CTAs of a cluster.
+SKINNY_TMS = (16, 32, 64)
+SKINNY_N = 128
+SKINNY_STAGES = (4, 6, 8, 10, 12)
+SKINNY_SPLITS = (1, 2, 4, 8)
 
 # Epilogue staging: 4 warps x 2 buffers x [32 rows x 64 cols] fp16.
 EPI_STAGING_BYTES = 4 * 2 * 32 * 64 * 2
@@ -69,8 +82,15 @@ OUT_DIR = Path(__file__).resolve().parent.parent / "csrc" / "generated"
 Cfg = Tuple[int, int, int, int, int, int, int, int]
 
 
+def is_skinny(tile_m: int) -> bool:
+    return tile_m in SKINNY_TMS
+
+
 def smem_bytes(tile_m: int, tile_n: int, tile_k: int, stages: int, mma_sm: int = 1) -> int:
-    """Dynamic shared memory of one CTA; mirrors SmemPlan in gemm_sm100_kernel.cuh."""
+    """Dynamic shared memory of one CTA; mirrors SmemPlan in gemm_sm100_kernel.cuh
+    (SkinnyPlan in gemm_skinny_kernel.cuh for tile_m < 128)."""
+    if is_skinny(tile_m):
+        return stages * (tile_k * tile_n * 2 + tile_m * tile_k * 2) + (2 * stages + 1) * 8 + 16 + ALIGN_SLACK
     a = (tile_m // mma_sm) * tile_k * 2
     b = tile_k * (tile_n // mma_sm) * 2
     return stages * (a + b) + EPI_STAGING_BYTES + 2 * stages * 8 + BARRIER_BYTES_FIXED + ALIGN_SLACK
@@ -87,6 +107,11 @@ def tmem_cols(tile_n: int) -> int:
 
 def valid(cfg: Sequence[int]) -> bool:
     tile_m, tile_n, tile_k, stages, mma_sm, raster, group, split_k = cfg
+    if is_skinny(tile_m):
+        # one cluster per (tile_m x 128) block of C; raster and group do not apply
+        return (tile_n == SKINNY_N and tile_k == 64 and mma_sm == 1 and raster == 0 and group == 1
+                and stages in SKINNY_STAGES and split_k in SKINNY_SPLITS
+                and smem_bytes(tile_m, tile_n, tile_k, stages) <= SMEM_CAP)
     if mma_sm not in (1, 2) or tile_m != BM_PER_SM * mma_sm:
         return False
     if tile_n % (64 * mma_sm) != 0 or not (64 <= tile_n <= 256 or (tile_n == 512 and mma_sm == 2)):
@@ -114,8 +139,13 @@ def enumerate_menu() -> List[Cfg]:
 
 
 def variants(menu: Sequence[Cfg]) -> List[Tuple[int, int, int]]:
-    """Distinct compile-time (tile_n, stages, mma_sm) triples, sorted."""
-    return sorted({(c[1], c[3], c[4]) for c in menu})
+    """Distinct compile-time (tile_n, stages, mma_sm) triples of the main kernel, sorted."""
+    return sorted({(c[1], c[3], c[4]) for c in menu if not is_skinny(c[0])})
+
+
+def skinny_variants(menu: Sequence[Cfg]) -> List[Tuple[int, int]]:
+    """Distinct compile-time (tile_m, stages) pairs of the skinny kernel, sorted."""
+    return sorted({(c[0], c[3]) for c in menu if is_skinny(c[0])})
 
 
 def menu_index(menu: Sequence[Cfg]) -> Dict[Cfg, int]:
@@ -144,6 +174,17 @@ def render(menu: Sequence[Cfg]) -> Dict[str, str]:
         vl.append(f"IDB_VARIANT({bn}, {st}, {cg})\n")
     out["gemm_variants.inc"] = "".join(vl)
 
+    sv = skinny_variants(menu)
+    sl = [HEADER, "// One line per compiled (tile_m, stages) instantiation of the skinny kernel.\n"]
+    for tm, st in sv:
+        sl.append(f"IDB_SKINNY({tm}, {st})\n")
+    out["gemm_skinny_variants.inc"] = "".join(sl)
+    bl = [HEADER, '#include "../gemm_skinny_kernel.cuh"\n\n', "namespace idb {\n"]
+    for tm, st in sv:
+        bl.append(f"IDB_DEFINE_SKINNY({tm}, {st})\n")
+    bl.append("}  // namespace idb\n")
+    out["gemm_bank_skinny.cu"] = "".join(bl)
+
     for bn, cg in sorted({(v[0], v[2]) for v in vs}):
         bl = [HEADER, '#include "../gemm_bank_common.cuh"\n\n', "namespace idb {\n"]
         for b2, st, c2 in vs:
@@ -167,7 +208,7 @@ def write(out_dir: Path = OUT_DIR, check: bool = False) -> List[Path]:
             if not check:
                 path.write_text(text)
     if not check:
-        for stale in out_dir.glob("gemm_bank_bn*.cu"):
+        for stale in out_dir.glob("gemm_bank_*.cu"):
             if stale.name not in files:
                 stale.unlink()
                 changed.append(stale)
@@ -181,7 +222,8 @@ def main(argv: Sequence[str] | None = None) -> None:
     args = ap.parse_args(argv)
     menu = enumerate_menu()
     changed = write(args.out, check=args.check)
-    print(f"Generated {len(menu)} configs over {len(variants(menu))} kernel instantiations")
+    print(f"Generated {len(menu)} configs over {len(variants(menu)) + len(skinny_variants(menu))} kernel "
+          "instantiations")
     if args.check and changed:
         print("stale:", *[str(p) for p in changed])
         raise SystemExit(1)

@@ -61,3 +61,29 @@ def test_generated_files_up_to_date():
 def test_render_is_deterministic():
     m = gen.enumerate_menu()
     assert gen.render(m) == gen.render(list(m))
+
+
+def test_skinny_rules_and_variants():
+    assert gen.valid((16, 128, 64, 12, 1, 0, 1, 8))
+    assert gen.valid((64, 128, 64, 8, 1, 0, 1, 1))
+    assert not gen.valid((16, 128, 64, 12, 1, 0, 1, 3))   # cluster of 1, 2, 4 or 8 CTAs
+    assert not gen.valid((16, 256, 64, 12, 1, 0, 1, 1))   # 128 columns of C: the TMEM lanes
+    assert not gen.valid((64, 128, 64, 10, 1, 0, 1, 1))   # shared memory
+    assert not gen.valid((32, 128, 64, 8, 1, 1, 1, 1))    # raster / group do not apply
+    assert not gen.valid((32, 128, 64, 8, 2, 0, 1, 1))
+    assert gen.skinny_variants(gen.enumerate_menu()) == [
+        (16, 4), (16, 6), (16, 8), (16, 10), (16, 12), (32, 4), (32, 6), (32, 8), (32, 10), (64, 4), (64, 6), (64, 8)]
+    for tm, st in gen.skinny_variants(gen.enumerate_menu()):
+        assert gen.smem_bytes(tm, 128, 64, st) <= gen.SMEM_CAP
+
+
+def test_default_cfg_for_skinny_shapes():
+    from infinite_dreams import _capi
+    row = lambda M, N, K: _capi.menu_row(_capi.lib.gemm_default_cfg(M, N, K))
+    assert row(16, 14336, 4096) == (16, 128, 64, 12, 1, 0, 1, 1)   # 112 clusters: one wave already
+    assert row(16, 4096, 4096) == (16, 128, 64, 12, 1, 0, 1, 4)    # 32 blocks x 4 CTAs
+    assert row(1, 4096, 4096) == (16, 128, 64, 12, 1, 0, 1, 4)
+    assert row(33, 4096, 4096) == (64, 128, 64, 8, 1, 0, 1, 4)
+    assert row(64, 14336, 4096) == (64, 128, 64, 8, 1, 0, 1, 1)
+    assert row(7, 12288, 96) == (16, 128, 64, 12, 1, 0, 1, 1)     # 2 K blocks: no split
+    assert row(65, 4096, 4096)[0] == 128                            # above 64 rows: the main kernel
