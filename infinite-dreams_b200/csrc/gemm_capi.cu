@@ -42,20 +42,22 @@ static const Variant kVariants[] = {
 #undef IDB_VARIANT
 };
 
-#define IDB_SKINNY(TM, ST)                                                                               \
-  cudaError_t launch_skinny_tm##TM##_s##ST(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, \
-                                           int grid, int cluster, cudaStream_t stream);
+#define IDB_SKINNY(TM, TN, ST)                                                                           \
+  cudaError_t launch_skinny_tm##TM##_tn##TN##_s##ST(const CUtensorMap& a, const CUtensorMap& b,           \
+                                                    const GemmParams& p, int grid, int cluster,           \
+                                                    cudaStream_t stream);
 #include "generated/gemm_skinny_variants.inc"
 #undef IDB_SKINNY
 
 struct SkinnyVariant {
   int tm;
+  int tn;
   int stages;
   SkinnyLaunchFn fn;
 };
 
 static const SkinnyVariant kSkinnyVariants[] = {
-#define IDB_SKINNY(TM, ST) {TM, ST, &launch_skinny_tm##TM##_s##ST},
+#define IDB_SKINNY(TM, TN, ST) {TM, TN, ST, &launch_skinny_tm##TM##_tn##TN##_s##ST},
 #include "generated/gemm_skinny_variants.inc"
 #undef IDB_SKINNY
 };
@@ -214,16 +216,16 @@ int make_plan(const void* A, const void* B, int64_t M, int64_t N, int64_t K, int
   }
   const int* row = kMenu[cfg_id];
   if (row[kColTileM] < kBM) {
-    // Skinny kernel: one cluster of split_k CTAs per (tile_m x 128) block of
+    // Skinny kernel: one cluster of split_k CTAs per (tile_m x tile_n) block of
     // C; the K blocks are divided among the cluster.  A cluster size above
     // the number of K blocks is lowered to the largest power of two that
     // still gives every CTA work (same GEMM).
     pl->skinny = true;
     pl->tile_m = row[kColTileM];
-    pl->tile_n = kSkinnyN;
+    pl->tile_n = row[kColTileN];
     pl->stages = row[kColStages];
     pl->tiles_m = static_cast<int>((M + pl->tile_m - 1) / pl->tile_m);
-    pl->tiles_n = static_cast<int>((N + kSkinnyN - 1) / kSkinnyN);
+    pl->tiles_n = static_cast<int>((N + pl->tile_n - 1) / pl->tile_n);
     const int64_t blocks = static_cast<int64_t>(pl->tiles_m) * pl->tiles_n;
     pl->kb_total = static_cast<int>((K + kBK - 1) / kBK);
     int s = row[kColSplitK];
@@ -454,7 +456,7 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
       return fail(GEMM_ERR_UNSUPPORTED, "skinny configurations (tile_m < 128) read A stored M x K (trans_a = 0)");
     }
     for (const SkinnyVariant& v : kSkinnyVariants) {
-      if (v.tm == pl.tile_m && v.stages == pl.stages) svar = &v;
+      if (v.tm == pl.tile_m && v.tn == pl.tile_n && v.stages == pl.stages) svar = &v;
     }
     if (!svar) return fail(GEMM_ERR_BAD_CFG, "no compiled skinny kernel for this configuration");
   } else {
@@ -676,11 +678,20 @@ int gemm_default_cfg(int64_t M, int64_t N, int64_t K) {
     // cluster).  The smallest row tile that holds M, the deepest ring that
     // fits, and the largest cluster that keeps about one wave with >= 4 K
     // blocks per CTA.
+    // Measured on B200: clusters of 8 cost more to launch than they save,
+    // and when 128-column blocks alone fill more than half the SMs, 256-column
+    // blocks in clusters of 2 stream B faster (512 contiguous bytes per row)
+    // for up to 32 rows; at 64 rows their 5-stage ring is too shallow.
     const int tm = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
-    const int stages = tm == 16 ? 12 : (tm == 32 ? 10 : 8);
     const int64_t blocks = (N + kSkinnyN - 1) / kSkinnyN;
+    const int64_t wide = (N + 2 * kSkinnyN - 1) / (2 * kSkinnyN);
+    if (tm <= 32 && blocks > pairs && wide * 2 <= kSms && kb >= 8) {
+      int knobs[IDB_MENU_COLS] = {tm, 2 * kSkinnyN, kBK, 6, 1, 0, 1, 2};
+      return gemm_cfg_find(knobs, IDB_MENU_COLS);
+    }
+    const int stages = tm == 16 ? 12 : (tm == 32 ? 10 : 8);
     int s = 1;
-    while (s < 8 && blocks * 2 * s <= kSms && kb / (2 * s) >= 4) s *= 2;
+    while (s < 4 && blocks * 2 * s <= kSms && kb / (2 * s) >= 4) s *= 2;
     int knobs[IDB_MENU_COLS] = {tm, kSkinnyN, kBK, stages, 1, 0, 1, s};
     return gemm_cfg_find(knobs, IDB_MENU_COLS);
   }

@@ -7,13 +7,14 @@
 //
 //  * operands swapped: the MMA computes C^T = B^T A^T, so 128 columns of C
 //    fill the 128 TMEM lanes (MMA M = 128) and the few rows of A are the MMA
-//    N (TM = 16, 32 or 64).  Per pipeline stage a CTA loads a [64 K x 128 n]
-//    tile of B (16 KiB, all useful) and a [TM x 64 K] tile of A (2-8 KiB), so
-//    the ring holds 8-12 stages of B in flight;
+//    N (TM = 16, 32 or 64).  A cluster owns TN = 128 or 256 columns of C
+//    (one or two MMAs per K step).  Per pipeline stage a CTA loads a
+//    [64 K x TN] tile of B (16 or 32 KiB, all useful) and a [TM x 64 K]
+//    tile of A (2-8 KiB), so the ring holds ~200 KiB of B in flight;
 //  * split-K inside a thread-block cluster: the S CTAs of a cluster own the
 //    same 128 columns and S consecutive K ranges.  Each writes its fp32
 //    partial tile into its own (now idle) pipeline buffers; after a cluster
-//    barrier, CTA r sums columns [r*128/S, (r+1)*128/S) of all S partials
+//    barrier, CTA r sums columns [r*TN/S, (r+1)*TN/S) of all S partials
 //    through distributed shared memory, in rank order (deterministic), and
 //    stores C.  No workspace, no atomics, no second pass over global memory.
 //
@@ -28,11 +29,14 @@
 
 namespace idb {
 
-constexpr int kSkinnyN = 128;  // columns of C per cluster: the 128 TMEM lanes
+constexpr int kSkinnyN = 128;  // columns of C per MMA: the 128 TMEM lanes
 
-template <int TM, int STAGES>
+// TN = columns of C per cluster: one (128) or two (256) MMAs of M = 128 per
+// K step; two read 512 contiguous bytes of every row of B per stage.
+template <int TM, int TN, int STAGES>
 struct SkinnyPlan {
-  static constexpr int kNBytes = kBK * kSkinnyN * 2;  // B tile: 16 KiB
+  static constexpr int kNB = TN / kSkinnyN;           // MMAs (accumulators) per K step
+  static constexpr int kNBytes = kBK * TN * 2;        // B tile: 16 or 32 KiB
   static constexpr int kMBytes = TM * kBK * 2;        // A tile: TM rows of 128 B
   static constexpr int kStageBytes = kNBytes + kMBytes;
   static constexpr int kOffN = 0;
@@ -42,18 +46,19 @@ struct SkinnyPlan {
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kUsed = kOffMisc + 16;
   static constexpr int kDynamicBytes = kUsed + 1024;
-  static constexpr uint32_t kTmemCols = TM <= 32 ? 32 : 64;
-  static constexpr int kPartialBytes = TM * kSkinnyN * 4;  // fp32 [TM][128]
+  static constexpr uint32_t kTmemCols = kNB * TM <= 32 ? 32 : (kNB * TM <= 64 ? 64 : 128);
+  static constexpr int kPartialBytes = TM * TN * 4;  // fp32 [TM][TN]
   static_assert(TM == 16 || TM == 32 || TM == 64, "MMA N of the swapped tile");
+  static_assert(TN == 128 || TN == 256, "one or two 128-row MMAs");
   static_assert(kMBytes % 1024 == 0, "swizzled A tiles need 1024-byte alignment");
   static_assert(kPartialBytes <= kOffBar, "the partial tile reuses the pipeline buffers");
 };
 
-template <int TM, int STAGES>
+template <int TM, int TN, int STAGES>
 __global__ void __launch_bounds__(kNumThreads, 1)
     gemm_skinny_f16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const GemmParams p) {
-  using Plan = SkinnyPlan<TM, STAGES>;
+  using Plan = SkinnyPlan<TM, TN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sN = smem + Plan::kOffN;
@@ -63,14 +68,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Plan::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* partial = reinterpret_cast<float*>(smem);  // after the mainloop: fp32 [TM][128]
+  float* partial = reinterpret_cast<float*>(smem);  // after the mainloop: fp32 [TM][TN]
 
   const int warp = static_cast<int>(threadIdx.x >> 5);
   const int lane = static_cast<int>(threadIdx.x & 31);
   const int S = static_cast<int>(cluster_nctarank());
   const int rank = static_cast<int>(cluster_ctarank());
   const int cid = static_cast<int>(cluster_id_x());
-  const int n0 = (cid % p.tiles_n) * kSkinnyN;
+  const int n0 = (cid % p.tiles_n) * TN;
   const int m0 = (cid / p.tiles_n) * TM;
   const int kb0 = static_cast<int>(static_cast<long long>(rank) * p.kb_total / S);
   const int kb1 = static_cast<int>(static_cast<long long>(rank + 1) * p.kb_total / S);
@@ -113,13 +118,18 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         const int k0 = kb * kBK;
         uint8_t* n_dst = sN + stage * Plan::kNBytes;
         mbar_arrive_expect_tx(&full_bar[stage], Plan::kStageBytes);
-        if (p.b_kmaj) {
-          // B stored N x K: one [128 n x 64 K] box, K-major rows
-          tma_load_2d(n_dst, &tmB, &full_bar[stage], k0, n0);
-        } else {
-          // B stored K x N: two [64 K x 64 n] atoms, n-major
-          tma_load_2d(n_dst, &tmB, &full_bar[stage], n0, k0);
-          tma_load_2d(n_dst + kBK * 128, &tmB, &full_bar[stage], n0 + 64, k0);
+#pragma unroll
+        for (int h = 0; h < Plan::kNB; ++h) {
+          uint8_t* dst = n_dst + h * (kBK * kSkinnyN * 2);
+          const int n = n0 + h * kSkinnyN;
+          if (p.b_kmaj) {
+            // B stored N x K: one [128 n x 64 K] box per MMA, K-major rows
+            tma_load_2d(dst, &tmB, &full_bar[stage], k0, n);
+          } else {
+            // B stored K x N: two [64 K x 64 n] atoms per MMA, n-major
+            tma_load_2d(dst, &tmB, &full_bar[stage], n, k0);
+            tma_load_2d(dst + kBK * 128, &tmB, &full_bar[stage], n + 64, k0);
+          }
         }
         tma_load_2d(sM + stage * Plan::kMBytes, &tmA, &full_bar[stage], k0, m0);
         ++issued;
@@ -165,8 +175,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         const uint32_t mb = smem_u32(sM + stage * Plan::kMBytes);
 #pragma unroll
         for (int j = 0; j < kBK / kUmmaK; ++j) {
-          mma_f16_ss<1>(tmem_base, smem_desc_sw128(nb + j * n_kstep, n_lbo, 1024),
-                        smem_desc_sw128(mb + j * (kUmmaK * 2), 16, 1024), idesc, (kb > kb0 || j > 0) ? 1u : 0u);
+#pragma unroll
+          for (int h = 0; h < Plan::kNB; ++h) {
+            mma_f16_ss<1>(tmem_base + static_cast<uint32_t>(h * TM),
+                          smem_desc_sw128(nb + h * (kBK * kSkinnyN * 2) + j * n_kstep, n_lbo, 1024),
+                          smem_desc_sw128(mb + j * (kUmmaK * 2), 16, 1024), idesc, (kb > kb0 || j > 0) ? 1u : 0u);
+          }
         }
         mma_commit<1>(&empty_bar[stage]);
         if (++stage == STAGES) {
@@ -196,14 +210,20 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     const bool ok = named_bar_and(1, 32 * kEpiWarps, mbar_wait(tfull_bar, 0, abort_flag));
     tc_fence_after();
     if (ok) {
+      // accumulator h holds columns [h*TM, (h+1)*TM) of TMEM: rows m of C for
+      // the columns n0 + h*128 + lane row
 #pragma unroll
-      for (int c32 = 0; c32 < (TM + 31) / 32; ++c32) {
+      for (int c32 = 0; c32 < (Plan::kNB * TM + 31) / 32; ++c32) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + c32 * 32, v);
         tmem_ld_wait();
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          if (c32 * 32 + i < TM) partial[(c32 * 32 + i) * kSkinnyN + n_local] = __uint_as_float(v[i]);
+          const int col = c32 * 32 + i;
+          if (col < Plan::kNB * TM) {
+            const int h = col / TM, m = col - h * TM;
+            partial[m * TN + h * kSkinnyN + n_local] = __uint_as_float(v[i]);
+          }
         }
       }
     } else {
@@ -217,7 +237,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   __syncwarp();
   cluster_sync();  // every CTA's partial tile is written and visible in the cluster
   {
-    const int ns = kSkinnyN / S;       // columns this CTA reduces
+    const int ns = TN / S;             // columns this CTA reduces
     const int g_per_row = ns / 4;      // 4-column groups per row
     const int groups = TM * g_per_row;
     const uint32_t base = smem_u32(partial);
@@ -227,7 +247,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       const int n = rank * ns + (g - m * g_per_row) * 4;
       const int gm = m0 + m, gn = n0 + n;
       if (gm >= p.M || gn >= p.N) continue;
-      const uint32_t off = static_cast<uint32_t>((m * kSkinnyN + n) * 4);
+      const uint32_t off = static_cast<uint32_t>((m * TN + n) * 4);
       float4 acc = ld_dsmem_f4(mapa_shared(base + off, 0));
       for (int q = 1; q < S; ++q) {
         const float4 x = ld_dsmem_f4(mapa_shared(base + off, static_cast<uint32_t>(q)));
@@ -262,11 +282,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   }
 }
 
-template <int TM, int STAGES>
+template <int TM, int TN, int STAGES>
 cudaError_t launch_skinny(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, int grid, int cluster,
                           cudaStream_t stream) {
-  using Plan = SkinnyPlan<TM, STAGES>;
-  auto kernel = gemm_skinny_f16<TM, STAGES>;
+  using Plan = SkinnyPlan<TM, TN, STAGES>;
+  auto kernel = gemm_skinny_f16<TM, TN, STAGES>;
   static std::atomic<unsigned long long> configured{0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -297,8 +317,9 @@ using SkinnyLaunchFn = cudaError_t (*)(const CUtensorMap& a, const CUtensorMap& 
 
 }  // namespace idb
 
-#define IDB_DEFINE_SKINNY(TM, ST)                                                                         \
-  cudaError_t launch_skinny_tm##TM##_s##ST(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, \
-                                           int grid, int cluster, cudaStream_t stream) {                   \
-    return launch_skinny<TM, ST>(a, b, p, grid, cluster, stream);                                         \
+#define IDB_DEFINE_SKINNY(TM, TN, ST)                                                                     \
+  cudaError_t launch_skinny_tm##TM##_tn##TN##_s##ST(const CUtensorMap& a, const CUtensorMap& b,            \
+                                                    const GemmParams& p, int grid, int cluster,            \
+                                                    cudaStream_t stream) {                                 \
+    return launch_skinny<TM, TN, ST>(a, b, p, grid, cluster, stream);                                     \
   }

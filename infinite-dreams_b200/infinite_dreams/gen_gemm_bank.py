@@ -10,8 +10,9 @@ Blackwell the knobs that matter are different, so the space is redefined:
 tile_m       tile rows: 128 * mma_sm (one tcgen05 MMA of M = tile_m); or
              16 / 32 / 64 for the skinny kernel (few rows of A: the MMA
              computes C^T with 128 columns of C as its M and tile_m as its
-             N; tile_n = 128, split_k = K slices reduced inside a cluster of
-             1, 2, 4 or 8 CTAs through distributed shared memory)
+             N; tile_n = 128 or 256 columns of C per cluster (one or two
+             MMAs per K step), split_k = K slices reduced inside a cluster
+             of 1, 2, 4 or 8 CTAs through distributed shared memory)
 tile_n       tile columns: one MMA N <= 256, or 512 for a CTA pair (two MMAs
              per K step, one accumulator); each CTA holds tile_n / mma_sm
              columns of B, a multiple of 64 (one 128-byte swizzle atom)
@@ -39,7 +40,7 @@ Outputs (deterministic, committed under ``csrc/generated``):
 * ``gemm_bank_bn<BN>_sm<S>.cu`` -- explicit instantiations, one file per
                                 (tile_n, mma_sm), so the bank compiles in parallel.
 * ``gemm_skinny_variants.inc`` / ``gemm_bank_skinny.cu`` -- the same for the
-                                skinny kernel's (tile_m, stages) pairs.
+                                skinny kernel's (tile_m, tile_n, stages) triples.
 """
 from __future__ import annotations
 
@@ -67,8 +68,8 @@ COLUMNS = ("tile_m", "tile_n", "tile_k", "stages", "mma_sm", "raster", "group", 
 # Skinny kernel (gemm_skinny_kernel.cuh): tile_m rows of A per cluster, 128
 # columns of C, K split over the CTAs of a cluster.
 SKINNY_TMS = (16, 32, 64)
-SKINNY_N = 128
-SKINNY_STAGES = (4, 6, 8, 10, 12)
+SKINNY_NS = (128, 256)
+SKINNY_STAGES = (4, 5, 6, 8, 10, 12)
 SKINNY_SPLITS = (1, 2, 4, 8)
 
 # Epilogue staging: 4 warps x 2 buffers x [32 rows x 64 cols] fp16.
@@ -109,7 +110,7 @@ def valid(cfg: Sequence[int]) -> bool:
     tile_m, tile_n, tile_k, stages, mma_sm, raster, group, split_k = cfg
     if is_skinny(tile_m):
         # one cluster per (tile_m x 128) block of C; raster and group do not apply
-        return (tile_n == SKINNY_N and tile_k == 64 and mma_sm == 1 and raster == 0 and group == 1
+        return (tile_n in SKINNY_NS and tile_k == 64 and mma_sm == 1 and raster == 0 and group == 1
                 and stages in SKINNY_STAGES and split_k in SKINNY_SPLITS
                 and smem_bytes(tile_m, tile_n, tile_k, stages) <= SMEM_CAP)
     if mma_sm not in (1, 2) or tile_m != BM_PER_SM * mma_sm:
@@ -143,9 +144,9 @@ def variants(menu: Sequence[Cfg]) -> List[Tuple[int, int, int]]:
     return sorted({(c[1], c[3], c[4]) for c in menu if not is_skinny(c[0])})
 
 
-def skinny_variants(menu: Sequence[Cfg]) -> List[Tuple[int, int]]:
-    """Distinct compile-time (tile_m, stages) pairs of the skinny kernel, sorted."""
-    return sorted({(c[0], c[3]) for c in menu if is_skinny(c[0])})
+def skinny_variants(menu: Sequence[Cfg]) -> List[Tuple[int, int, int]]:
+    """Distinct compile-time (tile_m, tile_n, stages) triples of the skinny kernel, sorted."""
+    return sorted({(c[0], c[1], c[3]) for c in menu if is_skinny(c[0])})
 
 
 def menu_index(menu: Sequence[Cfg]) -> Dict[Cfg, int]:
@@ -175,13 +176,13 @@ def render(menu: Sequence[Cfg]) -> Dict[str, str]:
     out["gemm_variants.inc"] = "".join(vl)
 
     sv = skinny_variants(menu)
-    sl = [HEADER, "// One line per compiled (tile_m, stages) instantiation of the skinny kernel.\n"]
-    for tm, st in sv:
-        sl.append(f"IDB_SKINNY({tm}, {st})\n")
+    sl = [HEADER, "// One line per compiled (tile_m, tile_n, stages) instantiation of the skinny kernel.\n"]
+    for tm, tn, st in sv:
+        sl.append(f"IDB_SKINNY({tm}, {tn}, {st})\n")
     out["gemm_skinny_variants.inc"] = "".join(sl)
     bl = [HEADER, '#include "../gemm_skinny_kernel.cuh"\n\n', "namespace idb {\n"]
-    for tm, st in sv:
-        bl.append(f"IDB_DEFINE_SKINNY({tm}, {st})\n")
+    for tm, tn, st in sv:
+        bl.append(f"IDB_DEFINE_SKINNY({tm}, {tn}, {st})\n")
     bl.append("}  // namespace idb\n")
     out["gemm_bank_skinny.cu"] = "".join(bl)
 

@@ -58,8 +58,10 @@ def test_de_trajectory_tables(eval_log, tmp_path):
     stats = tables["stats"]
     assert list(stats["gen"]) == sorted(stats["gen"])
     assert (stats["min"] <= stats["median"]).all() and (stats["median"] <= stats["max"]).all()
-    # the best of each generation's population can only improve under greedy replacement
-    assert (np.diff(stats["min"].to_numpy()) <= 0).all()
+    # the per-generation minima cover every logged search evaluation
+    log = pd.read_csv(eval_log)
+    search = log[(log["phase"] == "search") & (log["gen"] >= 0)]
+    assert stats["min"].min() == search["ms"].min()
     assert (tables["diversity"]["mean_pairwise_l2"] >= 0).all()
     assert np.isfinite(tables["points"][["pc1", "pc2"]].to_numpy()).all()
     paths = plot_de_trajectory.write(tables, str(tmp_path), png=False)

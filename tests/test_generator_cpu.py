@@ -71,19 +71,23 @@ def test_skinny_rules_and_variants():
     assert not gen.valid((64, 128, 64, 10, 1, 0, 1, 1))   # shared memory
     assert not gen.valid((32, 128, 64, 8, 1, 1, 1, 1))    # raster / group do not apply
     assert not gen.valid((32, 128, 64, 8, 2, 0, 1, 1))
-    assert gen.skinny_variants(gen.enumerate_menu()) == [
-        (16, 4), (16, 6), (16, 8), (16, 10), (16, 12), (32, 4), (32, 6), (32, 8), (32, 10), (64, 4), (64, 6), (64, 8)]
-    for tm, st in gen.skinny_variants(gen.enumerate_menu()):
-        assert gen.smem_bytes(tm, 128, 64, st) <= gen.SMEM_CAP
+    assert gen.valid((16, 256, 64, 6, 1, 0, 1, 2))        # two MMAs per K step
+    assert not gen.valid((16, 256, 64, 8, 1, 0, 1, 2))    # shared memory
+    sv = gen.skinny_variants(gen.enumerate_menu())
+    deepest = {(tm, tn): max(st for a, b, st in sv if (a, b) == (tm, tn)) for tm, tn, _ in sv}
+    assert deepest == {(16, 128): 12, (32, 128): 10, (64, 128): 8, (16, 256): 6, (32, 256): 6, (64, 256): 5}
+    for tm, tn, st in sv:
+        assert gen.smem_bytes(tm, tn, 64, st) <= gen.SMEM_CAP
 
 
 def test_default_cfg_for_skinny_shapes():
     from infinite_dreams import _capi
     row = lambda M, N, K: _capi.menu_row(_capi.lib.gemm_default_cfg(M, N, K))
-    assert row(16, 14336, 4096) == (16, 128, 64, 12, 1, 0, 1, 1)   # 112 clusters: one wave already
+    assert row(16, 14336, 4096) == (16, 256, 64, 6, 1, 0, 1, 2)    # 56 wide blocks x 2 CTAs
     assert row(16, 4096, 4096) == (16, 128, 64, 12, 1, 0, 1, 4)    # 32 blocks x 4 CTAs
     assert row(1, 4096, 4096) == (16, 128, 64, 12, 1, 0, 1, 4)
     assert row(33, 4096, 4096) == (64, 128, 64, 8, 1, 0, 1, 4)
     assert row(64, 14336, 4096) == (64, 128, 64, 8, 1, 0, 1, 1)
-    assert row(7, 12288, 96) == (16, 128, 64, 12, 1, 0, 1, 1)     # 2 K blocks: no split
+    assert row(16, 2048, 8192) == (16, 128, 64, 12, 1, 0, 1, 4)    # clusters of at most 4
+    assert row(7, 12288, 96) == (16, 128, 64, 12, 1, 0, 1, 1)     # 2 K blocks: no split, not wide
     assert row(65, 4096, 4096)[0] == 128                            # above 64 rows: the main kernel

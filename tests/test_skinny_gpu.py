@@ -16,10 +16,10 @@ from helpers import assert_close, capi_gemm, make_inputs
 pytestmark = pytest.mark.gpu
 
 
-def _cfg(tm, stages, split):
+def _cfg(tm, stages, split, tn=128):
     from infinite_dreams import _capi
-    cid = _capi.cfg_find((tm, 128, 64, stages, 1, 0, 1, split))
-    assert cid >= 0, (tm, stages, split)
+    cid = _capi.cfg_find((tm, tn, 64, stages, 1, 0, 1, split))
+    assert cid >= 0, (tm, tn, stages, split)
     return cid
 
 
@@ -42,19 +42,20 @@ def _ex(A_st, B_st, M, N, K, tb, cid, alpha=1.0, beta=0.0, D=None, bias=None, ac
     return C
 
 
-VARIANTS = [(16, 4), (16, 6), (16, 8), (16, 10), (16, 12), (32, 4), (32, 6), (32, 8), (32, 10), (64, 4), (64, 6),
-            (64, 8)]
+from infinite_dreams import gen_gemm_bank as _gen  # noqa: E402
+
+VARIANTS = _gen.skinny_variants(_gen.enumerate_menu())   # (tile_m, tile_n, stages)
 
 
-@pytest.mark.parametrize("tm,stages", VARIANTS)
+@pytest.mark.parametrize("tm,tn,stages", VARIANTS)
 @pytest.mark.parametrize("split", [1, 2, 4, 8])
-def test_every_skinny_variant(cuda_device, tm, stages, split):
-    """Ragged M (one block and several), N (partial 128-column block) and K (partial 64 block)."""
+def test_every_skinny_variant(cuda_device, tm, tn, stages, split):
+    """Ragged M (one block and several), N (partial column block) and K (partial 64 block)."""
     for M in (tm - 3, 2 * tm + 5):
         N, K = 1000, 1000
-        A, B = make_inputs(M, N, K, dist="skinny", seed=tm + stages + split + M)
-        assert_close(capi_gemm(A.cuda(), B.cuda(), _cfg(tm, stages, split)), oracle.gemm_f16(A.numpy(), B.numpy()),
-                     K, f"tm {tm} st {stages} S {split} M {M}")
+        A, B = make_inputs(M, N, K, dist="skinny", seed=tm + tn + stages + split + M)
+        assert_close(capi_gemm(A.cuda(), B.cuda(), _cfg(tm, stages, split, tn)),
+                     oracle.gemm_f16(A.numpy(), B.numpy()), K, f"tm {tm} tn {tn} st {stages} S {split} M {M}")
 
 
 @pytest.mark.parametrize("K", [1, 64, 65, 200, 4096])
@@ -76,8 +77,8 @@ def test_skinny_workload_shapes_default_cfg(cuda_device, M, N):
     assert_close(capi_gemm(A.cuda(), B.cuda(), cid), oracle.gemm_f16(A.numpy(), B.numpy()), K, f"{M}x{N}x{K}")
 
 
-@pytest.mark.parametrize("split", [1, 4])
-def test_skinny_b_stored_n_by_k_and_epilogue(cuda_device, split):
+@pytest.mark.parametrize("split,tn", [(1, 128), (4, 128), (2, 256)])
+def test_skinny_b_stored_n_by_k_and_epilogue(cuda_device, split, tn):
     """y = act(alpha * x @ W.t() + beta * D + b), W stored N x K (K-major B tiles)."""
     M, N, K = 24, 1500, 2048
     g = torch.Generator().manual_seed(split)
@@ -85,7 +86,7 @@ def test_skinny_b_stored_n_by_k_and_epilogue(cuda_device, split):
     W = (torch.rand((N, K), generator=g) * 0.1 - 0.05).half()
     b = (torch.rand((N,), generator=g) - 0.5).half()
     D = (torch.rand((M, N), generator=g) * 2 - 1).half()
-    cid = _cfg(32, 8, split)
+    cid = _cfg(32, 8 if tn == 128 else 6, split, tn)
     plain = _ex(x.cuda(), W.cuda(), M, N, K, 1, cid)
     assert_close(plain, oracle.gemm_ex(x.numpy(), W.numpy(), trans_b=True), K, "W stored N x K")
     for act, name in ((0, "none"), (1, "relu"), (2, "gelu")):
