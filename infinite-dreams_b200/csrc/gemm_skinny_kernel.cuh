@@ -31,8 +31,9 @@ namespace idb {
 
 constexpr int kSkinnyN = 128;  // columns of C per MMA: the 128 TMEM lanes
 
-// TN = columns of C per cluster: one (128) or two (256) MMAs of M = 128 per
-// K step; two read 512 contiguous bytes of every row of B per stage.
+// TN = columns of C per cluster: one, two or four MMAs of M = 128 per K step
+// (128, 256 or 512 columns); a wider block reads more contiguous bytes of
+// every row of B per stage (256 B, 512 B, 1 KiB).
 template <int TM, int TN, int STAGES>
 struct SkinnyPlan {
   static constexpr int kNB = TN / kSkinnyN;           // MMAs (accumulators) per K step
@@ -46,10 +47,11 @@ struct SkinnyPlan {
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kUsed = kOffMisc + 16;
   static constexpr int kDynamicBytes = kUsed + 1024;
-  static constexpr uint32_t kTmemCols = kNB * TM <= 32 ? 32 : (kNB * TM <= 64 ? 64 : 128);
+  static constexpr uint32_t kTmemCols =
+      kNB * TM <= 32 ? 32 : (kNB * TM <= 64 ? 64 : (kNB * TM <= 128 ? 128 : 256));
   static constexpr int kPartialBytes = TM * TN * 4;  // fp32 [TM][TN]
   static_assert(TM == 16 || TM == 32 || TM == 64, "MMA N of the swapped tile");
-  static_assert(TN == 128 || TN == 256, "one or two 128-row MMAs");
+  static_assert(TN == 128 || TN == 256 || TN == 512, "one, two or four 128-row MMAs");
   static_assert(kMBytes % 1024 == 0, "swizzled A tiles need 1024-byte alignment");
   static_assert(kPartialBytes <= kOffBar, "the partial tile reuses the pipeline buffers");
 };
@@ -207,7 +209,13 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     // ------------------------------------------------------------ accumulator -> partial tile
     const int ew = warp & 3;
     const int n_local = ew * 32 + lane;
-    const bool ok = named_bar_and(1, 32 * kEpiWarps, mbar_wait(tfull_bar, 0, abort_flag));
+    // One lane per warp polls the barrier through the whole mainloop; the
+    // others wait at the shuffle instead of competing for issue slots with
+    // the producer and MMA threads.
+    bool got = true;
+    if (lane == 0) got = mbar_wait(tfull_bar, 0, abort_flag);
+    got = __shfl_sync(0xffffffffu, got ? 1 : 0, 0) != 0;
+    const bool ok = named_bar_and(1, 32 * kEpiWarps, got);
     tc_fence_after();
     if (ok) {
       // accumulator h holds columns [h*TM, (h+1)*TM) of TMEM: rows m of C for

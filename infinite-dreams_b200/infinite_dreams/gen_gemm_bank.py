@@ -10,8 +10,8 @@ Blackwell the knobs that matter are different, so the space is redefined:
 tile_m       tile rows: 128 * mma_sm (one tcgen05 MMA of M = tile_m); or
              16 / 32 / 64 for the skinny kernel (few rows of A: the MMA
              computes C^T with 128 columns of C as its M and tile_m as its
-             N; tile_n = 128 or 256 columns of C per cluster (one or two
-             MMAs per K step), split_k = K slices reduced inside a cluster
+             N; tile_n = 128, 256 or 512 columns of C per cluster (one,
+             two or four MMAs per K step), split_k = K slices reduced inside a cluster
              of 1, 2, 4 or 8 CTAs through distributed shared memory)
 tile_n       tile columns: one MMA N <= 256, or 512 for a CTA pair (two MMAs
              per K step, one accumulator); each CTA holds tile_n / mma_sm
@@ -68,8 +68,8 @@ COLUMNS = ("tile_m", "tile_n", "tile_k", "stages", "mma_sm", "raster", "group", 
 # Skinny kernel (gemm_skinny_kernel.cuh): tile_m rows of A per cluster, 128
 # columns of C, K split over the CTAs of a cluster.
 SKINNY_TMS = (16, 32, 64)
-SKINNY_NS = (128, 256)
-SKINNY_STAGES = (4, 5, 6, 8, 10, 12)
+SKINNY_NS = (128, 256, 512)
+SKINNY_STAGES = (3, 4, 5, 6, 8, 10, 12)
 SKINNY_SPLITS = (1, 2, 4, 8)
 
 # Epilogue staging: 4 warps x 2 buffers x [32 rows x 64 cols] fp16.

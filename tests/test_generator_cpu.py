@@ -75,7 +75,8 @@ def test_skinny_rules_and_variants():
     assert not gen.valid((16, 256, 64, 8, 1, 0, 1, 2))    # shared memory
     sv = gen.skinny_variants(gen.enumerate_menu())
     deepest = {(tm, tn): max(st for a, b, st in sv if (a, b) == (tm, tn)) for tm, tn, _ in sv}
-    assert deepest == {(16, 128): 12, (32, 128): 10, (64, 128): 8, (16, 256): 6, (32, 256): 6, (64, 256): 5}
+    assert deepest == {(16, 128): 12, (32, 128): 10, (64, 128): 8, (16, 256): 6, (32, 256): 6, (64, 256): 5,
+                       (16, 512): 3, (32, 512): 3, (64, 512): 3}
     for tm, tn, st in sv:
         assert gen.smem_bytes(tm, tn, 64, st) <= gen.SMEM_CAP
 
