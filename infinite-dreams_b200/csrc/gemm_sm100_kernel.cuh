@@ -201,8 +201,9 @@ __device__ __forceinline__ bool work_next(const GemmParams& p, int worker, int w
     w.tile = u / p.split_k;
     w.part = u - w.tile * p.split_k;
     w.nparts = p.split_k;
-    w.kb0 = static_cast<int>((static_cast<long long>(w.part) * kbt) / p.split_k);
-    w.kb1 = static_cast<int>((static_cast<long long>(w.part + 1) * kbt) / p.split_k);
+    // part * kb_total < 16 * 2^25 fits 32 bits (K < 2^31, split_k <= 16)
+    w.kb0 = static_cast<int>(static_cast<unsigned>(w.part * kbt) / static_cast<unsigned>(p.split_k));
+    w.kb1 = static_cast<int>(static_cast<unsigned>((w.part + 1) * kbt) / static_cast<unsigned>(p.split_k));
     w.down = (it.count & 1) != 0;
     it.cur += workers;
   }
@@ -436,7 +437,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const int cluster_id = static_cast<int>(blockIdx.x) / CG;
   const int num_clusters = static_cast<int>(gridDim.x) / CG;
 
-  if (threadIdx.x == 0) {
+  // Barriers are set up by the first epilogue thread, so that the producer
+  // thread can work out its first unit meanwhile (below).
+  if (threadIdx.x == 64) {
 #pragma unroll
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
@@ -452,12 +455,20 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     *last_flag = 0;
     fence_mbar_init();
   }
+  // The first work unit of the producer and MMA threads is computed while
+  // the barriers and TMEM are being set up, so the first TMA load and the
+  // first MMA follow the sync without delay.
+  WorkIter first_wi = work_begin(p, cluster_id, num_clusters);
+  Unit first_w;
+  bool first_have = false;
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
     if (p.c_tma) prefetch_tmap(&tmC);
   }
+  if (warp < 2 && lane == 0) first_have = work_next(p, cluster_id, num_clusters, first_wi, first_w);
   if (warp == 1) {
+    __syncwarp();  // tcgen05.alloc is warp-wide (.sync.aligned)
     tmem_alloc<CG>(tmem_slot, Plan::kTmemCols);
     tmem_relinquish<CG>();
   }
@@ -474,9 +485,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      WorkIter wi = work_begin(p, cluster_id, num_clusters);
-      Unit w;
-      while (ok && work_next(p, cluster_id, num_clusters, wi, w)) {
+      WorkIter& wi = first_wi;
+      Unit& w = first_w;
+      for (bool have = first_have; ok && have; have = work_next(p, cluster_id, num_clusters, wi, w)) {
         const int arow = w.tm * (kBM * CG) + static_cast<int>(rank) * kBM;
         // this CTA's B columns: its share of every MMA's N range
         const int bcol = w.tn * BN + static_cast<int>(rank) * Plan::kMmaNc;
@@ -571,9 +582,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      WorkIter wi = work_begin(p, cluster_id, num_clusters);
-      Unit w;
-      while (ok && work_next(p, cluster_id, num_clusters, wi, w)) {
+      WorkIter& wi = first_wi;
+      Unit& w = first_w;
+      for (bool have = first_have; ok && have; have = work_next(p, cluster_id, num_clusters, wi, w)) {
         const int kb0 = w.kb0, kb1 = w.kb1;
         // the first kNumAcc units use accumulators that have never been used
         // A single accumulator made of two MMA halves (512-column tiles) is
