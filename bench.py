@@ -6,7 +6,9 @@ N contiguous row blocks, one per rank (one process per GPU); B is generated on
 rank 0 and broadcast once at set-up (untimed); each rank computes its C rows
 with no data-path collective.  Total work is fixed, so scaling is "strong".
 A "step" is one GEMM over the local row block.  The optional NCCL all-gather
-of C (``--allgather``) is timed separately and reported under "allgather".
+of C (``--allgather``) is timed separately and reported under "allgather": as a
+GEMM followed by one NCCL all-gather, as a two-chunk pipeline of both, and
+fused into the GEMM (tiles stored into every rank's C over NVLink).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
   torchrun --nproc-per-node N bench.py --gpus N ...
@@ -394,14 +396,24 @@ def run_ours(args: argparse.Namespace) -> None:
                          compute=lambda a, b, o: ext.gemm_forward_cfg(
                              a, b, dispatch.lookup(a.shape[0], b.shape[1], a.shape[1]), out=o))
 
+        def fused():
+            # every tile goes to all ranks' C from the GEMM's epilogue (NVLink stores), then a
+            # one-element all-reduce on the stream marks all ranks' grids complete
+            sharded_gemm(A, B, M_total=size, gather=True, exchange="fused")
+
         ms_one = timed(one_shot)
         ms_pipe = timed(pipelined)
+        ms_fused = timed(fused)
         allgather = {"ms_per_step_gemm_then_allgather": ms_one,
                      "value_gemm_then_allgather": 2.0 * size ** 3 / (ms_one * 1e-3) / 1e12,
                      "ms_per_step_pipelined_2_chunks": ms_pipe,
                      "value_pipelined": 2.0 * size ** 3 / (ms_pipe * 1e-3) / 1e12,
+                     "ms_per_step_fused": ms_fused,
+                     "value_fused": 2.0 * size ** 3 / (ms_fused * 1e-3) / 1e12,
                      "bytes_received_per_rank": (world - 1) * rows * N * 2, "steps": n_ag}
         del Cfull
+        from infinite_dreams.sharded import release_peer_buffers
+        release_peer_buffers()
 
     # End to end through the public op.  Every step copies its own inputs from
     # pinned host memory and reads its result back; copies run on their own

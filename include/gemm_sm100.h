@@ -124,6 +124,34 @@ int gemm_launch_ex(const void* A, const void* B, void* C, int64_t M, int64_t N, 
 size_t gemm_workspace_bytes_ex(const void* A, const void* B, int64_t M, int64_t N, int64_t K, int64_t lda,
                                int64_t ldb, int trans_a, int trans_b, int cfg_id);
 
+/* Fused all-gather for M-row sharding over the GPUs of one node (one
+ * process per GPU).  Same as gemm_launch, and each finished tile of C is
+ * also stored, over NVLink, at the same offset and pitch ldc into
+ * peer_C[0..n_peers) -- the copies of the full C on the other GPUs (opened
+ * with gemm_ipc_import), already offset to this rank's rows.  The transfer
+ * overlaps the GEMM tile by tile.  The caller learns that every peer has
+ * finished writing into its own C from a collective issued after the
+ * launch on the same stream (the stream orders it after this grid on every
+ * rank).  n_peers <= GEMM_MAX_PEERS; the configuration must have
+ * tile_m >= 128 and split_k = 1 (GEMM_ERR_UNSUPPORTED otherwise).
+ * Extends the reference, which ran on one GPU; replaces a separate NCCL
+ * all-gather of the C row blocks. */
+#define GEMM_MAX_PEERS 7
+int gemm_launch_gather(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                       int64_t ldb, int64_t ldc, const void* const* peer_C, int n_peers, int cfg_id,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* CUDA IPC of device memory between the processes of one node, for
+ * gemm_launch_gather.  gemm_ipc_export writes the GEMM_IPC_HANDLE_BYTES-byte
+ * handle of the allocation that holds ptr and ptr's offset inside it;
+ * another process passes both to gemm_ipc_import to map that memory (peer
+ * access enabled) and gets the same address in its own space;
+ * gemm_ipc_close unmaps it.  No counterpart in the reference. */
+#define GEMM_IPC_HANDLE_BYTES 64
+int gemm_ipc_export(const void* ptr, void* handle, int64_t* offset);
+int gemm_ipc_import(const void* handle, int64_t offset, void** ptr);
+int gemm_ipc_close(void* ptr);
+
 /* A reasonable configuration for a shape when no tuned entry exists.
  * No counterpart in the reference (its tuner had no per-shape dispatch). */
 int gemm_default_cfg(int64_t M, int64_t N, int64_t K);

@@ -13,6 +13,7 @@
 
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
 
@@ -201,6 +202,8 @@ struct OpDesc {
   int64_t ldd = 0;
   const void* bias = nullptr;
   int act = 0;
+  const void* const* peers = nullptr;  // fused all-gather targets (gemm_launch_gather)
+  int n_peers = 0;
   bool epi() const { return alpha != 1.0f || beta != 0.0f || bias != nullptr || act != 0; }
 };
 
@@ -401,6 +404,15 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
   if (op.bias && reinterpret_cast<uintptr_t>(op.bias) % 2u) {
     return fail(GEMM_ERR_INVALID_ARG, "bias must be 2-byte aligned (fp16)");
   }
+  if (op.n_peers < 0 || op.n_peers > kMaxPeers || (op.n_peers > 0 && !op.peers)) {
+    return fail(GEMM_ERR_INVALID_ARG, "n_peers must be in [0, " + std::to_string(kMaxPeers) +
+                                          "] with a peer pointer array");
+  }
+  for (int i = 0; i < op.n_peers; ++i) {
+    if (!op.peers[i] || reinterpret_cast<uintptr_t>(op.peers[i]) % 2u) {
+      return fail(GEMM_ERR_INVALID_ARG, "peer C pointers must be non-null and 2-byte aligned");
+    }
+  }
   if (cfg_id < 0 || cfg_id >= IDB_MENU_SIZE) {
     return fail(GEMM_ERR_BAD_CFG, "cfg_id " + std::to_string(cfg_id) + " out of range [0, " +
                                       std::to_string(IDB_MENU_SIZE) + ")");
@@ -427,6 +439,14 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
   p.D = op.beta != 0.0f ? static_cast<const __half*>(op.D) : nullptr;
   p.ldd = op.beta != 0.0f ? op.ldd : 0;
   p.bias = static_cast<const __half*>(op.bias);
+  p.n_peers = op.n_peers;
+  for (int i = 0; i < kMaxPeers; ++i) {
+    p.peer_C[i] = i < op.n_peers ? static_cast<__half*>(const_cast<void*>(op.peers[i])) : nullptr;
+  }
+  if (op.n_peers > 0 && (pl.skinny || pl.max_parts > 1 || K == 0)) {
+    return fail(GEMM_ERR_UNSUPPORTED, "the fused all-gather needs K > 0 and a configuration without split-K / "
+                                      "stream-K and with tile_m >= 128");
+  }
   if (K == 0) {
     // Empty reduction: C = 0 (the reference kernel's loop body never runs),
     // or act(beta * D + bias) with a fused epilogue.
@@ -563,6 +583,10 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
 
 void record_last_error(const std::string& msg) { t_last_error = msg; }
 
+// Imported peer pointer -> base of the opened allocation (for gemm_ipc_close).
+std::mutex g_ipc_mu;
+std::map<void*, void*>* g_ipc_bases = new std::map<void*, void*>();
+
 }  // namespace idb
 
 using namespace idb;
@@ -648,6 +672,72 @@ int gemm_launch_ex(const void* A, const void* B, void* C, int64_t M, int64_t N, 
   op.bias = bias;
   op.act = activation;
   return launch_impl(A, B, C, M, N, K, lda, ldb, ldc, op, cfg_id, workspace, workspace_bytes, stream);
+}
+
+int gemm_launch_gather(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                       int64_t ldb, int64_t ldc, const void* const* peer_C, int n_peers, int cfg_id, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  t_last_error.clear();
+  OpDesc op;
+  op.peers = peer_C;
+  op.n_peers = n_peers;
+  return launch_impl(A, B, C, M, N, K, lda, ldb, ldc, op, cfg_id, workspace, workspace_bytes, stream);
+}
+
+int gemm_ipc_export(const void* ptr, void* handle, int64_t* offset) {
+  t_last_error.clear();
+  if (!ptr || !handle || !offset) return fail(GEMM_ERR_INVALID_ARG, "ptr, handle and offset must be non-null");
+  // The handle names the whole allocation that holds ptr; the offset locates ptr in it.
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  using RangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static RangeFn range = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      return static_cast<RangeFn>(nullptr);
+    }
+    return reinterpret_cast<RangeFn>(f);
+  }();
+  if (!range) return fail(GEMM_ERR_CUDA, "cuMemGetAddressRange is not available from the driver");
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) {
+    return fail(GEMM_ERR_INVALID_ARG, "ptr is not device memory of this process");
+  }
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return fail_cuda(e, "cudaIpcGetMemHandle");
+  std::memcpy(handle, &h, sizeof(h));
+  *offset = static_cast<int64_t>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+  return GEMM_OK;
+}
+
+int gemm_ipc_import(const void* handle, int64_t offset, void** ptr) {
+  t_last_error.clear();
+  if (!handle || !ptr || offset < 0) return fail(GEMM_ERR_INVALID_ARG, "handle and ptr must be non-null, offset >= 0");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaIpcOpenMemHandle");
+  *ptr = static_cast<uint8_t*>(base) + offset;
+  std::lock_guard<std::mutex> lock(g_ipc_mu);
+  (*g_ipc_bases)[*ptr] = base;
+  return GEMM_OK;
+}
+
+int gemm_ipc_close(void* ptr) {
+  t_last_error.clear();
+  void* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_ipc_mu);
+    auto it = g_ipc_bases->find(ptr);
+    if (it == g_ipc_bases->end()) return fail(GEMM_ERR_INVALID_ARG, "ptr was not returned by gemm_ipc_import");
+    base = it->second;
+    g_ipc_bases->erase(it);
+  }
+  cudaError_t e = cudaIpcCloseMemHandle(base);
+  return e == cudaSuccess ? GEMM_OK : fail_cuda(e, "cudaIpcCloseMemHandle");
 }
 
 int gemm_launch_knobs(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,

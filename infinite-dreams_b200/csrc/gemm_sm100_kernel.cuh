@@ -50,6 +50,7 @@ constexpr int kNumThreads = 64 + 32 * kEpiWarps;
 constexpr int kStoreRows = 32;    // rows per epilogue store box (one warp's TMEM lanes)
 constexpr int kStoreCols = 64;    // columns per epilogue store box (128 bytes)
 constexpr int kCounterSlots = 65536;  // split-K tile tickets at the head of the workspace
+constexpr int kMaxPeers = 7;          // peer copies of C (fused all-gather over 8 GPUs)
 
 struct GemmParams {
   int M, N, K;
@@ -82,6 +83,11 @@ struct GemmParams {
   const __half* D;
   long long ldd;
   const __half* bias;
+  // Fused all-gather: each finished box of C is also stored into the C of
+  // every peer GPU (peer_C[i]: that GPU's copy at this rank's offset, same
+  // pitch ldc), over NVLink, right after it is staged.  Non-split configs.
+  int n_peers;
+  __half* peer_C[kMaxPeers];
 };
 
 template <int BN, int STAGES, int CG>
@@ -382,6 +388,34 @@ __device__ __forceinline__ void reduce_partials(const GemmParams& p, const float
       } else {
         const float vals[4] = {acc[b].x, acc[b].y, acc[b].z, acc[b].w};
         for (int c = 0; c < 4 && gc + c < p.N; ++c) dst[c] = __float2half_rn(vals[c]);
+      }
+    }
+  }
+}
+
+// Copies one staged [32 x 64] box (128-byte swizzled, as stage_row_sw128
+// left it) to the same place in every peer's C: in step i lane l moves the
+// 16 bytes of row 4i + l/8, segment l%8, so each store instruction writes
+// four whole 128-byte rows of every peer.
+__device__ __forceinline__ void copy_box_to_peers(const GemmParams& p, const uint8_t* buf, int row0, int col0,
+                                                  int lane) {
+  const int seg = lane & 7;
+  const int c = col0 + seg * 8;
+  const bool vec = (static_cast<uintptr_t>(p.ldc * 2) & 15u) == 0;
+#pragma unroll 2
+  for (int i = 0; i < 8; ++i) {
+    const int r = 4 * i + (lane >> 3);
+    const int gr = row0 + r;
+    if (gr >= p.M || c >= p.N) continue;
+    const uint4 v = *reinterpret_cast<const uint4*>(buf + r * 128 + ((seg ^ (r & 7)) << 4));
+    const long long off = static_cast<long long>(gr) * p.ldc + c;
+    for (int q = 0; q < p.n_peers; ++q) {
+      __half* dst = p.peer_C[q] + off;
+      if (vec && c + 8 <= p.N && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+        *reinterpret_cast<uint4*>(dst) = v;
+      } else {
+        const __half* h = reinterpret_cast<const __half*>(&v);
+        for (int e = 0; e < 8 && c + e < p.N; ++e) dst[e] = h[e];
       }
     }
   }
@@ -840,6 +874,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             }
             __syncwarp();
           }
+          if (p.n_peers > 0) {
+            __syncwarp();  // every lane's row is staged
+            copy_box_to_peers(p, buf, row0, col0, lane);
+            __syncwarp();
+          }
           cb ^= 1;
           if (kHalvesEpi && c64 == (BN / 64) / 2 - 1) {
             // first MMA half read out: the next unit's MMAs may start on it
@@ -865,6 +904,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     // The staging smem must stay valid until the last TMA stores have read it;
     // their global writes complete with the grid.
     if (p.c_tma && lane == 0) bulk_wait_group_read<0>();
+    // Peer stores are ordered before anything this thread does later (the
+    // grid's completion, which the ranks then agree on through NCCL).
+    if (p.n_peers > 0) __threadfence_system();
   }
 
   // ------------------------------------------------------------ teardown

@@ -20,6 +20,9 @@ GEMM_ERR_CUDA = 4
 GEMM_ERR_UNSUPPORTED = 5
 GEMM_ERR_DEVICE_TIMEOUT = 6
 
+GEMM_MAX_PEERS = 7
+GEMM_IPC_HANDLE_BYTES = 64
+
 GEMM_ACT_NONE = 0
 GEMM_ACT_RELU = 1
 GEMM_ACT_GELU = 2
@@ -47,6 +50,12 @@ _SIG = [
       _P, _I64, _P, ctypes.c_int, ctypes.c_int, _P, ctypes.c_size_t, _P]),
     ("gemm_workspace_bytes_ex", ctypes.c_size_t,
      [_P, _P, _I64, _I64, _I64, _I64, _I64, ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    ("gemm_launch_gather", ctypes.c_int,
+     [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_int,
+      _P, ctypes.c_size_t, _P]),
+    ("gemm_ipc_export", ctypes.c_int, [_P, _P, ctypes.POINTER(ctypes.c_int64)]),
+    ("gemm_ipc_import", ctypes.c_int, [_P, _I64, ctypes.POINTER(ctypes.c_void_p)]),
+    ("gemm_ipc_close", ctypes.c_int, [_P]),
     ("gemm_default_cfg", ctypes.c_int, [_I64, _I64, _I64]),
     ("gemm_device_error", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
     ("gemm_last_error", ctypes.c_char_p, []),

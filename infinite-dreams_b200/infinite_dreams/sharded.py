@@ -12,11 +12,20 @@ rank's block is cut into row chunks, each chunk's GEMM writes straight into
 its rows of the full C, and that chunk's all-gather runs (asynchronously)
 while the next chunk is computed.
 
-Only NCCL moves remote data: no kernel here reads another GPU's memory.
+``exchange="fused"`` folds the all-gather into the GEMM: every rank keeps a
+full-size C whose memory the other ranks map once (CUDA IPC), and the
+kernel's epilogue stores each finished tile both locally and, over NVLink,
+into every peer's copy (``gemm_launch_gather``), so the transfer overlaps
+the remaining tiles' mainloop.  A one-element NCCL all-reduce issued after
+the launch on the same stream marks the point where every rank's grid, and
+with it every write into this rank's C, has completed.  No kernel reads
+another GPU's memory; peers are only written to.
 """
 from __future__ import annotations
 
-from typing import Callable, Optional, Tuple
+import ctypes
+import threading
+from typing import Callable, Dict, List, Optional, Tuple
 
 import torch
 import torch.distributed as dist
@@ -46,14 +55,25 @@ def _default_compute(A: torch.Tensor, B: torch.Tensor, out: Optional[torch.Tenso
 def sharded_gemm(A_local: torch.Tensor, B: torch.Tensor, M_total: Optional[int] = None, gather: bool = False,
                  group=None, out: Optional[torch.Tensor] = None,
                  compute: Optional[Callable[[torch.Tensor, torch.Tensor, Optional[torch.Tensor]], torch.Tensor]] = None,
-                 chunks: int = 1) -> torch.Tensor:
+                 chunks: int = 1, exchange: str = "nccl") -> torch.Tensor:
     """This rank's rows of C = A @ B (or all of C when gather=True).
 
     A_local holds this rank's row block (``row_block``); B is the full
     replicated K x N operand.  ``compute`` defaults to the dispatched
     kernel-bank GEMM.  ``chunks`` > 1 overlaps the all-gather with the
     compute (equal row blocks only; other cases fall back to one exchange).
+    ``exchange="fused"`` (gather=True, CUDA, equal row blocks) writes every
+    tile to all ranks from inside the GEMM; the returned full C is a buffer
+    owned by this module: it stays intact until the second fused call of
+    that shape after this one, provided whatever reads it is issued on the
+    calling stream before the next fused call.
     """
+    if exchange not in ("nccl", "fused"):
+        raise ValueError("exchange must be 'nccl' or 'fused'")
+    if exchange == "fused" and gather and dist.is_initialized() and dist.get_world_size(group) > 1:
+        if out is not None or compute is not None:
+            raise ValueError("exchange='fused' owns its output buffer and runs the kernel bank itself")
+        return _fused_gather(A_local, B, M_total, group)
     compute = compute or _default_compute
     if gather and chunks > 1 and dist.is_initialized() and dist.get_world_size(group) > 1:
         full = _pipelined_gather(A_local, B, M_total, group, out, compute, chunks)
@@ -124,3 +144,145 @@ def _pipelined_gather(A_local: torch.Tensor, B: torch.Tensor, M_total: Optional[
     for w in works:
         w.wait()
     return full
+
+
+# ---------------------------------------------------------------- fused all-gather
+
+_ipc_lock = threading.Lock()
+# (rows, N, device, group key) -> two (full C buffer, [peer base pointer or None per rank]) pairs used
+# alternately, and the index of the next one
+_fused_buffers: Dict[Tuple[int, int, int, int], list] = {}
+
+
+def _group_key(group) -> int:
+    return 0 if group is None else id(group)
+
+
+def _equal_rows(rows: int, device: torch.device, group) -> bool:
+    world = dist.get_world_size(group)
+    sizes = torch.tensor([rows], device=device, dtype=torch.int64)
+    all_sizes = [torch.zeros_like(sizes) for _ in range(world)]
+    dist.all_gather(all_sizes, sizes, group=group)
+    return all(int(s.item()) == rows for s in all_sizes)
+
+
+def _fused_buffer(rows: int, N: int, device: torch.device, group) -> Tuple[torch.Tensor, List[Optional[int]]]:
+    """This rank's full C for the next fused call and the other ranks' copies of it, mapped here.
+
+    Two buffers per shape are used in turn.  Peers write a call's tiles into
+    this rank's buffer while this rank may still be reading the previous
+    call's result; the buffer they write was last read before the previous
+    call's closing all-reduce, which every rank's stream has passed before
+    any peer's kernel of this call starts.  So a result stays intact until
+    the call after next, provided work that reads it is issued on the calling
+    stream before the next fused call.
+
+    The buffers are set up on the first call for a shape, which also checks
+    (collectively) that every rank has the same number of rows; later calls
+    of that shape take no collective step here, so every rank must keep
+    passing equal row blocks."""
+    key = (rows, N, device.index, _group_key(group))
+    with _ipc_lock:
+        entry = _fused_buffers.get(key)
+    if entry is None:
+        if not _equal_rows(rows, device, group):
+            raise ValueError("exchange='fused' needs equal row blocks on every rank")
+        entry = [_share_buffer(rows, N, device, group), _share_buffer(rows, N, device, group), 0]
+        with _ipc_lock:
+            _fused_buffers[key] = entry
+    pair = entry[entry[2]]
+    entry[2] ^= 1
+    return pair
+
+
+def _share_buffer(rows: int, N: int, device: torch.device, group) -> Tuple[torch.Tensor, List[Optional[int]]]:
+    """A new full-size C on this rank, and every other rank's one mapped into this process."""
+    from . import _capi
+
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    if world - 1 > _capi.GEMM_MAX_PEERS:
+        raise ValueError(f"the fused all-gather supports at most {_capi.GEMM_MAX_PEERS + 1} ranks")
+    full = torch.empty((rows * world, N), dtype=torch.float16, device=device)
+    handle = (ctypes.c_char * _capi.GEMM_IPC_HANDLE_BYTES)()
+    offset = ctypes.c_int64(0)
+    _capi.check(_capi.lib.gemm_ipc_export(full.data_ptr(), handle, ctypes.byref(offset)), "gemm_ipc_export")
+    shared: List[Optional[Tuple[bytes, int]]] = [None] * world
+    dist.all_gather_object(shared, (bytes(handle), offset.value), group=group)
+    peers: List[Optional[int]] = []
+    for r, (h, off) in enumerate(shared):
+        if r == rank:
+            peers.append(None)
+            continue
+        ptr = ctypes.c_void_p()
+        _capi.check(_capi.lib.gemm_ipc_import(h, off, ctypes.byref(ptr)), "gemm_ipc_import")
+        peers.append(int(ptr.value))
+    return full, peers
+
+
+def _gather_cfg(rows: int, N: int, K: int) -> int:
+    """The dispatched config when the fused all-gather supports it (tile_m >= 128, no split-K), else a
+    CTA-pair (or, for few rows, 1-CTA) tile without split."""
+    from . import _capi, dispatch
+
+    cid = dispatch.lookup(rows, N, K)
+    knobs = _capi.menu_row(cid)
+    if knobs[0] >= 128 and knobs[7] == 1:
+        return cid
+    fallback = (256, 256, 64, 4, 2, 0, 8, 1) if rows >= 256 else (128, 128, 64, 4, 1, 0, 8, 1)
+    return _capi.cfg_find(fallback)
+
+
+def _fused_gather(A_local: torch.Tensor, B: torch.Tensor, M_total: Optional[int], group) -> torch.Tensor:
+    from . import _capi, infinite_dreams_ext as ext
+
+    if not (A_local.is_cuda and B.is_cuda):
+        raise ValueError("exchange='fused' needs CUDA tensors")
+    ext._check_inputs(A_local, B)
+    device = A_local.device
+    rows, K = int(A_local.shape[0]), int(A_local.shape[1])
+    N = int(B.shape[1])
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    if M_total is not None and int(M_total) != rows * world:
+        raise ValueError(f"row blocks sum to {rows * world}, expected {M_total}")
+    A_local, B = A_local.contiguous(), B.contiguous()
+    full, peers = _fused_buffer(rows, N, device, group)   # raises on unequal row blocks
+    mine = full[rank * rows:(rank + 1) * rows]
+    offset = rank * rows * N * 2
+    targets = [p + offset for p in peers if p is not None]
+    arr = (ctypes.c_void_p * max(len(targets), 1))(*targets)
+    cid = _gather_cfg(rows, N, K)
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device)
+        need = _capi.lib.gemm_workspace_bytes(A_local.data_ptr(), B.data_ptr(), rows, N, K, K, N, cid)
+        ws_ptr, ws_len = ext._workspace(device, stream, need) if need else (0, 0)
+        _capi.check(_capi.lib.gemm_launch_gather(A_local.data_ptr(), B.data_ptr(), mine.data_ptr(), rows, N, K, K, N,
+                                                 N, arr, len(targets), cid, ws_ptr or None, ws_len,
+                                                 stream.cuda_stream or None), "gemm_launch_gather")
+        # Ordered after this rank's grid on its stream: completes once every
+        # rank's grid (and so every write into this rank's C) has finished.
+        done = torch.zeros(1, dtype=torch.float32, device=device)
+        dist.all_reduce(done, group=group)
+    return full
+
+
+def release_peer_buffers(group=None) -> None:
+    """Unmaps the peers' buffers and drops the fused all-gather's own buffers.
+
+    Collective: every rank calls it (before destroying the process group), so
+    that no rank frees memory another rank still has mapped."""
+    from . import _capi
+
+    with _ipc_lock:
+        items = [(k, v) for k, v in _fused_buffers.items() if k[3] == _group_key(group)]
+    if not items:
+        return
+    torch.cuda.synchronize()
+    for _, entry in items:
+        for _, peers in entry[:2]:
+            for ptr in peers:
+                if ptr is not None:
+                    _capi.check(_capi.lib.gemm_ipc_close(ptr), "gemm_ipc_close")
+    dist.barrier(group=group)
+    with _ipc_lock:
+        for k, _ in items:
+            _fused_buffers.pop(k, None)

@@ -31,7 +31,7 @@ def _worker(rank, world, port, M, N, K, q):
     import torch.distributed as dist
 
     from helpers import make_inputs
-    from infinite_dreams.sharded import broadcast_b, row_block, sharded_gemm
+    from infinite_dreams.sharded import broadcast_b, release_peer_buffers, row_block, sharded_gemm
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
@@ -42,9 +42,26 @@ def _worker(rank, world, port, M, N, K, q):
         Bd = B.to(dev) if rank == 0 else torch.zeros((K, N), dtype=torch.float16, device=dev)
         broadcast_b(Bd)
         r0, r1 = row_block(M, world, rank)
-        C = sharded_gemm(A[r0:r1].contiguous().to(dev), Bd, M_total=M, gather=True)
+        A_local = A[r0:r1].contiguous().to(dev)
+        C = sharded_gemm(A_local, Bd, M_total=M, gather=True)
         torch.cuda.synchronize()
-        q.put((rank, C.cpu().numpy().view(np.uint16)))
+        fused = []
+        if M % world == 0:
+            # tiles written into every rank's C over NVLink by the GEMM itself; three calls, so that
+            # one of the two alternating buffers is reused after being overwritten with NaN
+            for _ in range(3):
+                F = sharded_gemm(A_local, Bd, M_total=M, gather=True, exchange="fused")
+                torch.cuda.synchronize()
+                fused.append(F.cpu().numpy().view(np.uint16).copy())
+                F.fill_(float("nan"))   # the next call must rewrite every element
+        else:
+            try:
+                sharded_gemm(A_local, Bd, M_total=M, gather=True, exchange="fused")
+                fused.append("accepted unequal blocks")
+            except ValueError:
+                pass
+        q.put((rank, C.cpu().numpy().view(np.uint16), fused))
+        release_peer_buffers()
         dist.barrier(device_ids=[rank])
     finally:
         dist.destroy_process_group()
@@ -70,7 +87,13 @@ def test_sharded_gemm_nccl_allgather(cuda_device, M):
     A, B = make_inputs(M, N, K, seed=5)
     ref = oracle_gemm(A, B).astype(np.float32)
     tol = 1e-2 * np.sqrt(K / 1024) * np.abs(ref).max() + 1e-3
-    for rank, c in results:
+    for rank, c, fused in results:
         got = c.view(np.float16).astype(np.float32)
         assert got.shape == ref.shape
         assert np.abs(got - ref).max() <= tol, rank
+        for f in fused:
+            assert not isinstance(f, str), f
+            g = f.view(np.float16).astype(np.float32)
+            assert g.shape == ref.shape and np.isfinite(g).all(), rank
+            assert np.abs(g - ref).max() <= tol, ("fused", rank)
+        assert len(fused) == (3 if M % world == 0 else 0)

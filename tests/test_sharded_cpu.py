@@ -50,6 +50,17 @@ def _worker(rank, world, port, M, N, K, q):
         local = sharded_gemm(A[r0:r1].contiguous(), B, compute=_cpu_compute)
         full = sharded_gemm(A[r0:r1].contiguous(), B, M_total=M, gather=True, compute=_cpu_compute)
         piped = sharded_gemm(A[r0:r1].contiguous(), B, M_total=M, gather=True, compute=_cpu_compute, chunks=3)
+        # the fused exchange writes into peers' GPU memory: refused for CPU tensors, and it owns its output
+        errors = []
+        for kw in (dict(exchange="fused"), dict(exchange="fused", compute=_cpu_compute), dict(exchange="ring")):
+            try:
+                sharded_gemm(A[r0:r1].contiguous(), B, M_total=M, gather=True, **kw)
+                errors.append(None)
+            except ValueError as e:
+                errors.append(str(e))
+        assert errors[0] is not None and "CUDA" in errors[0], errors
+        assert errors[1] is not None and "owns its output" in errors[1], errors
+        assert errors[2] is not None and "exchange must be" in errors[2], errors
         q.put((rank, local.numpy().view(np.uint16), full.numpy().view(np.uint16), (r0, r1),
                oracle.gemm_f16(A.numpy(), B.numpy()).view(np.uint16), piped.numpy().view(np.uint16)))
     finally:
