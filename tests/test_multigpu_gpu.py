@@ -69,7 +69,7 @@ def _worker(rank, world, port, M, N, K, q):
 
 @pytest.mark.parametrize("M", [2048, 1001])
 def test_sharded_gemm_nccl_allgather(cuda_device, M):
-    world = min(torch.cuda.device_count(), 4)
+    world = min(torch.cuda.device_count(), 8)
     if world < 2:
         pytest.skip("needs 2 or more GPUs")
     from helpers import make_inputs, oracle_gemm
