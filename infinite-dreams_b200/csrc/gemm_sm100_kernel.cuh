@@ -726,9 +726,13 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       const bool use_d = p.epi && p.beta != 0.0f;
       uint4 draw[8];
       if (use_d) load_d_box(p, tm * (kBM * CG) + static_cast<int>(rank) * kBM + ew * 32, tn * BN, lane, draw);
-      // All four warps take the same decision, so none is left waiting at a
-      // later named barrier if another gave up.
-      ok = named_bar_and(1, 32 * kEpiWarps, mbar_wait(&tfull_bar[acc], acc_phase, abort_flag));
+      // One lane per warp waits for the accumulator (the others wait at the
+      // shuffle); all four warps then take the same decision, so none is
+      // left waiting at a later named barrier if another gave up.
+      bool got = true;
+      if (lane == 0) got = mbar_wait(&tfull_bar[acc], acc_phase, abort_flag);
+      got = __shfl_sync(0xffffffffu, got ? 1 : 0, 0) != 0;
+      ok = named_bar_and(1, 32 * kEpiWarps, got);
       if (!ok) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + static_cast<uint32_t>(acc * BN);
