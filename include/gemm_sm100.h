@@ -163,6 +163,15 @@ int gemm_default_cfg(int64_t M, int64_t N, int64_t K);
  * src/gemm_ext.cpp:50). */
 int gemm_device_error(int device, int* code);
 
+/* Self-test of the kernels' bounded waits: launches one thread that waits on
+ * an mbarrier nothing completes, gives up after limit_ns (<= 1 s) exactly as
+ * the GEMM kernels' roles do, and sets an error bit in the device error word,
+ * which the next gemm_device_error reports (GEMM_ERR_DEVICE_TIMEOUT) and
+ * clears.  Synchronises the device; *waited_ns receives the time the wait
+ * took.  No fault, trap or hang is involved, and the context stays usable.
+ * No counterpart in the reference, which had no bounded waits. */
+int gemm_selftest_wait_timeout(uint64_t limit_ns, uint64_t* waited_ns);
+
 /* Size of the static scratch array behind gemm_launch_noalloc (32 MiB). */
 #define GEMM_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
 

@@ -89,6 +89,25 @@ __global__ void pack_rows_f16(const __half* __restrict__ src, long long lds, __h
 }
 
 
+// Self-test of the bounded waits: one thread waits on an mbarrier that
+// nothing will complete, gives up after limit_ns exactly as the GEMM
+// kernels' roles do, and records the error bit in the device error word.
+__global__ void bounded_wait_selftest(int* err, unsigned long long limit_ns, unsigned long long* waited_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint64_t t0 = globaltimer_ns();
+    if (!mbar_wait_limit(&bar, 0, &abort_flag, limit_ns)) atomicOr(err, kDevErrTimeoutSelfTest);
+    *waited_ns = globaltimer_ns() - t0;
+  }
+}
+
 // C = act(beta * D + bias) for an empty reduction (K = 0) with a fused
 // epilogue: the accumulator is 0, so alpha plays no part.
 __global__ void epilogue_only_f16(GemmParams p) {
@@ -822,6 +841,32 @@ int gemm_default_cfg(int64_t M, int64_t N, int64_t K) {
   }
   int knobs[IDB_MENU_COLS] = {kBM, tile_n, kBK, stages, 1, 0, 8, split};
   return gemm_cfg_find(knobs, IDB_MENU_COLS);
+}
+
+int gemm_selftest_wait_timeout(uint64_t limit_ns, uint64_t* waited_ns) {
+  t_last_error.clear();
+  if (limit_ns == 0 || limit_ns > 1000000000ull) {
+    return fail(GEMM_ERR_INVALID_ARG, "limit_ns must be in (0, 1e9]");
+  }
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(GEMM_ERR_UNSUPPORTED, "device index out of range");
+  std::call_once(g_err_once[dev], [dev] {
+    g_err_status[dev] = cudaGetSymbolAddress(reinterpret_cast<void**>(&g_err_word[dev]), g_device_error);
+  });
+  if (g_err_status[dev] != cudaSuccess) return fail_cuda(g_err_status[dev], "cudaGetSymbolAddress(g_device_error)");
+  unsigned long long* d_waited = nullptr;
+  e = cudaMalloc(&d_waited, sizeof(unsigned long long));
+  if (e != cudaSuccess) return fail_cuda(e, "cudaMalloc");
+  bounded_wait_selftest<<<1, 32>>>(g_err_word[dev], limit_ns, d_waited);
+  e = cudaGetLastError();
+  unsigned long long h = 0;
+  if (e == cudaSuccess) e = cudaMemcpy(&h, d_waited, sizeof(h), cudaMemcpyDeviceToHost);
+  cudaFree(d_waited);
+  if (e != cudaSuccess) return fail_cuda(e, "bounded_wait_selftest");
+  if (waited_ns) *waited_ns = h;
+  return GEMM_OK;
 }
 
 int gemm_device_error(int device, int* code) {

@@ -21,6 +21,7 @@ enum : int {
   kDevErrTimeoutMma = 1 << 1,
   kDevErrTimeoutEpilogue = 1 << 2,
   kDevErrTimeoutTeardown = 1 << 3,
+  kDevErrTimeoutSelfTest = 1 << 4,   // gemm_selftest_wait_timeout
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -80,18 +81,24 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
   return ok != 0;
 }
 
-// Wait until the phase with the given parity has completed.  Returns false on
-// timeout or when another role raised the CTA abort flag.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+// Wait until the phase with the given parity has completed.  Returns false
+// after `limit_ns` of %globaltimer time, or when another role raised the CTA
+// abort flag.
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
     if ((i & 7u) == 0u) {
       if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+      if (globaltimer_ns() - t0 > limit_ns) return false;
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  return mbar_wait_limit(bar, parity, abort_flag, kWaitLimitNs);
 }
 
 // ----------------------------------------------------------------- clusters

@@ -58,6 +58,7 @@ _SIG = [
     ("gemm_ipc_close", ctypes.c_int, [_P]),
     ("gemm_default_cfg", ctypes.c_int, [_I64, _I64, _I64]),
     ("gemm_device_error", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
+    ("gemm_selftest_wait_timeout", ctypes.c_int, [ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64)]),
     ("gemm_last_error", ctypes.c_char_p, []),
     ("gemm_status_string", ctypes.c_char_p, [ctypes.c_int]),
 ]

@@ -4,8 +4,9 @@ For each shape the dispatched configuration (tuned table entry, else the
 heuristic) is timed with distinct CUDA events, L2 flushed before every
 repetition (``ms``: one launch per repetition, so its launch latency is
 included), and back to back on warm caches (``ms_warm_b2b``, the reference
-tuner's method), on seeded inputs (uniform[-1,1]; skinny shapes A~N(0,1),
-B~N(0,0.02^2)).  The roofline time of a shape is
+tuner's method; it includes the host work of each call), and the same back
+to back replayed from a CUDA graph (``ms_graph_b2b``, device time only), on
+seeded inputs (uniform[-1,1]; skinny shapes A~N(0,1), B~N(0,0.02^2)).  The roofline time of a shape is
 max(2MNK / peak_flops, 2(MK+KN+MN) / peak_bw) with fp16 input/output bytes
 only; % of roofline = roofline time / measured time.  Both the nominal B200
 peaks (2250 TFLOP/s dense fp16, 8000 GB/s) and the measured ones
@@ -109,12 +110,14 @@ def run(sets: List[str], iters: int, warmup: int, cfg_override: Optional[int] = 
             # back-to-back launches on warm caches, the way the reference's
             # tuner timed its kernels (infinite_dreams/utils.py:13-27)
             ms_warm = time_cuda_ms(ours, iters=iters, warmup=warmup, flush_l2=False)
+            # the same launches replayed from a CUDA graph: no host work in between
+            ms_graph = time_cuda_ms(ours, iters=iters, warmup=warmup, graph=True)
             ms_torch = time_cuda_ms(theirs, iters=iters, warmup=warmup, flush_l2=True) if with_torch else None
             flops = 2.0 * M * N * K
             nbytes = 2.0 * (M * K + K * N + M * N)
             rows.append({
                 "set": name, "M": M, "N": N, "K": K, "layout": layout, "epilogue": epilogue, "cfg_id": cid,
-                "ms_torch_cublas": ms_torch,
+                "ms_torch_cublas": ms_torch, "ms_graph_b2b": ms_graph,
                 "knobs": dict(zip(ext.CFG_COLUMNS, table[cid].tolist())), "ms": ms, "ms_warm_b2b": ms_warm,
                 "tflops": flops / (ms * 1e-3) / 1e12, "gbs": nbytes / (ms * 1e-3) / 1e9,
                 "pct_fp16_peak_nominal": 100.0 * flops / (ms * 1e-3) / 1e12 / NOMINAL_TFLOPS,
@@ -148,7 +151,7 @@ def main(argv: Optional[List[str]] = None) -> None:
     for r in rows:
         tq = f" torch {r['ms_torch_cublas']:8.4f}" if r["ms_torch_cublas"] is not None else ""
         print(f"{r['set']:9s} {r['M']:6d} {r['N']:6d} {r['K']:6d} {r['layout']} {r['epilogue']:9s} "
-              f"{r['ms']:8.4f} ms (warm {r['ms_warm_b2b']:8.4f}){tq}  "
+              f"{r['ms']:8.4f} ms (warm {r['ms_warm_b2b']:8.4f}, graph {r['ms_graph_b2b']:8.4f}){tq}  "
               f"{r['tflops']:7.1f} TF/s "
               f"{r['gbs']:7.0f} GB/s  {r['pct_roofline_nominal']:5.1f}% roof(nom) "
               f"{r['pct_roofline_measured']:5.1f}% roof(meas)  {r['bound']}  {tuple(r['knobs'].values())}")

@@ -4,7 +4,9 @@
 with its timing bug fixed: the reference recorded start and stop on ONE event
 (``start = end = torch.cuda.Event(...)``, :19), so its elapsed time was ~0.
 Here start and stop are distinct events on the current stream, and an
-optional L2 flush separates repetitions for shapes whose operands fit in L2.
+optional L2 flush separates repetitions for shapes whose operands fit in L2,
+or the repetitions are replayed from a CUDA graph (no host work between
+launches).
 ``write_csv`` keeps the reference's field list (:30-42) and appends the
 Blackwell knob columns.
 """
@@ -39,11 +41,32 @@ def l2_flush(device: Optional[torch.device] = None) -> None:
 
 
 @torch.no_grad()
-def time_cuda_ms(fn: Callable[[], Any], iters: int, warmup: int, flush_l2: bool = False) -> float:
-    """Mean device milliseconds of ``fn`` over ``iters`` runs after ``warmup`` runs."""
+def time_cuda_ms(fn: Callable[[], Any], iters: int, warmup: int, flush_l2: bool = False,
+                 graph: bool = False) -> float:
+    """Mean device milliseconds of ``fn`` over ``iters`` runs after ``warmup`` runs.
+
+    ``graph=True``: the ``iters`` calls are recorded once into a CUDA graph
+    and the graph is replayed between the events, so launches follow each
+    other without any host work in between (device time back to back).
+    """
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(iters):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record()
+        g.replay()
+        end.record()
+        torch.cuda.synchronize()
+        del g
+        return start.elapsed_time(end) / max(iters, 1)
     if not flush_l2:
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)

@@ -100,3 +100,27 @@ def test_torch_binding_matches_ctypes_path(cuda_device):
             ext._fast = ext_fast
         assert torch.equal(y_fast.view(torch.int16), y_slow.view(torch.int16)), (M, N, K)
     ext.check_device_errors()
+
+
+def test_bounded_wait_times_out_and_the_context_survives(cuda_device):
+    """A wait on a barrier nothing completes gives up after its limit, the host reads the error bit
+    (GEMM_ERR_DEVICE_TIMEOUT), reading clears it, and GEMMs keep working on the same context."""
+    import ctypes
+    from infinite_dreams import _capi, infinite_dreams_ext as ext
+    lib = _capi.lib
+    code = ctypes.c_int(0)
+    assert lib.gemm_device_error(0, ctypes.byref(code)) == _capi.GEMM_OK and code.value == 0
+    waited = ctypes.c_uint64(0)
+    _capi.check(lib.gemm_selftest_wait_timeout(10_000_000, ctypes.byref(waited)), "gemm_selftest_wait_timeout")
+    assert 10_000_000 <= waited.value < 500_000_000, waited.value          # gave up after ~10 ms, not at once
+    assert lib.gemm_device_error(0, ctypes.byref(code)) == _capi.GEMM_ERR_DEVICE_TIMEOUT
+    assert code.value == 1 << 4                                            # the self-test's bit
+    with pytest.raises(_capi.GemmError):                                   # the op surface reports it the same way
+        lib.gemm_selftest_wait_timeout(10_000_000, ctypes.byref(waited))
+        ext.check_device_errors(0)
+    assert lib.gemm_device_error(0, ctypes.byref(code)) == _capi.GEMM_OK and code.value == 0
+    A, B = make_inputs(256, 384, 320, seed=3)
+    C = ext.gemm_forward_cfg(A.cuda(), B.cuda(), ext.default_cfg(256, 384, 320))
+    assert_close(C, oracle_gemm(A, B), 320, "after a timed-out wait")
+    ext.check_device_errors()
+    assert lib.gemm_selftest_wait_timeout(0, ctypes.byref(waited)) == _capi.GEMM_ERR_INVALID_ARG
