@@ -189,11 +189,6 @@ __device__ __forceinline__ void bulk_wait_group_read() {
   asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
 }
 
-template <int N>
-__device__ __forceinline__ void bulk_wait_group() {
-  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
-}
-
 // Make generic-proxy writes to shared memory visible to the async proxy
 // (TMA store / tcgen05.mma operand reads).
 __device__ __forceinline__ void fence_proxy_async_smem() {
