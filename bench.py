@@ -49,6 +49,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--size", type=int, default=SIZE, help="M = N = K of the workload")
     ap.add_argument("--cfg", type=int, default=None, help="menu cfg_id (default: dispatch table / heuristic)")
+    ap.add_argument("--knobs", type=str, default=None,
+                    help="kernel config as its knob tuple, e.g. 256,512,64,4,2,1,8,1 (stable across menu changes)")
     ap.add_argument("--allgather", action="store_true", help="also time the NCCL all-gather of C")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -307,7 +309,13 @@ def run_ours(args: argparse.Namespace) -> None:
     assert size % world == 0, "size must divide by the number of ranks"
     rows = size // world
     M, N, K = rows, size, size
-    cfg_id = args.cfg if args.cfg is not None else dispatch.lookup(M, N, K)
+    if args.knobs is not None:
+        from infinite_dreams import _capi
+        cfg_id = _capi.cfg_find([int(v) for v in args.knobs.split(",")])
+        if cfg_id < 0:
+            raise SystemExit(f"--knobs {args.knobs} is not in the kernel bank menu")
+    else:
+        cfg_id = args.cfg if args.cfg is not None else dispatch.lookup(M, N, K)
     knobs = dict(zip(ext.CFG_COLUMNS, ext.gemm_cfg_table_cpu()[cfg_id].tolist()))
 
     # inputs: rank r's A block comes from the seed (0, r); B from rank 0, broadcast
@@ -493,7 +501,9 @@ def run_ours(args: argparse.Namespace) -> None:
                 "frac": achieved / peak, "peak_source": f"{pk['source']} bf16 dense GEMM, sustained",
                 "frac_of_burst": achieved / float(pk["bf16_tflops"]),
                 "frac_of_nominal_2250": achieved / NOMINAL_FP16_TFLOPS,
-                "kernel": f"gemm_f16_sm100<{knobs['tile_n']},{knobs['stages']}>",
+                "kernel": (f"gemm_skinny_f16<{knobs['tile_m']},{knobs['tile_n']},{knobs['stages']}>"
+                           if knobs["tile_m"] < 128 else
+                           f"gemm_f16_sm100<{knobs['tile_n']},{knobs['stages']},{knobs['mma_sm']}>"),
                 "algorithmic_flop_per_launch": 2.0 * M * N * K, "launch_ms": kern_ms,
                 "traffic": traffic_for(size, world)}
     cpu = None
