@@ -292,8 +292,9 @@ int make_plan(const void* A, const void* B, int64_t M, int64_t N, int64_t K, int
     }
     pl->max_parts = static_cast<int>(mp);
   }
-  if (pl->max_parts > 1 && pl->num_tiles > kCounterSlots) {
-    return fail(GEMM_ERR_UNSUPPORTED, "split-K / stream-K support at most 65536 output tiles");
+  // tickets and partial slots per 128-row half of a tile (one per CTA of a pair)
+  if (pl->max_parts > 1 && static_cast<int64_t>(pl->num_tiles) * pl->cg > kCounterSlots) {
+    return fail(GEMM_ERR_UNSUPPORTED, "split-K / stream-K support at most 65536 output tile halves");
   }
   }
   pl->pack_a = M > 0 && K > 0 && !tma_addressable(A, lda);
@@ -302,7 +303,7 @@ int make_plan(const void* A, const void* B, int64_t M, int64_t N, int64_t K, int
   if (pl->max_parts > 1 || pl->pack_a || pl->pack_b) off = kCounterBytes;
   if (pl->max_parts > 1) {
     pl->off_partials = off;
-    off += static_cast<size_t>(pl->num_tiles) * pl->max_parts * kBM * pl->tile_n * sizeof(float);
+    off += static_cast<size_t>(pl->num_tiles) * pl->cg * pl->max_parts * kBM * pl->tile_n * sizeof(float);
     off = static_cast<size_t>(round_up(static_cast<int64_t>(off), 256));
   }
   // A packed copy keeps the operand's stored orientation (rows x cols below).

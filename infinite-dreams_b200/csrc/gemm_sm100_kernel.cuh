@@ -740,11 +740,16 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       const int grow = cta_row0 + row;
       const bool row_ok = grow < p.M;
       const int tile = w.tile;
-      const bool partial = (CG == 1) && (w.nparts > 1);
+      // Split tiles (split-K / stream-K): 1-CTA tiles, and CTA-pair tiles
+      // with two accumulators.  Each CTA of a pair owns the slots and ticket
+      // of its own 128 rows (slot tile = tile * CG + rank).
+      constexpr bool kSplitOK = (CG == 1) || (Plan::kNumAcc == 2);
+      const bool partial = kSplitOK && (w.nparts > 1);
+      const int slot_tile = tile * CG + static_cast<int>(rank);
       float* slots = nullptr;
       if (partial) {
         // 1. this CTA's K piece of the tile -> its partial slot (valid rows only)
-        slots = p.partials + static_cast<size_t>(tile) * p.max_parts * (kBM * BN);
+        slots = p.partials + static_cast<size_t>(slot_tile) * p.max_parts * (kBM * BN);
         float4* mine = reinterpret_cast<float4*>(slots + static_cast<size_t>(w.part) * (kBM * BN));
 #pragma unroll 1
         for (int c32 = 0; c32 < BN / 32; ++c32) {
@@ -764,7 +769,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         __threadfence();
         named_bar_sync(1, 32 * kEpiWarps);
         if (ticket_thread) {
-          const unsigned old = atomicAdd(&p.counters[tile], 1u);
+          const unsigned old = atomicAdd(&p.counters[slot_tile], 1u);
           *last_flag = (old == static_cast<unsigned>(w.nparts - 1)) ? 1 : 0;
         }
         named_bar_sync(1, 32 * kEpiWarps);
@@ -776,11 +781,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         if (!last || coop) {
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+          if (lane == 0) release_acc(acc);
           if (last) {
             __threadfence();
             reduce_partials<BN>(p, slots, w.nparts, cta_row0, tn * BN, static_cast<int>(threadIdx.x) - 64);
-            if (ticket_thread) p.counters[tile] = 0u;  // ticket zero for the next launch
+            if (ticket_thread) p.counters[slot_tile] = 0u;  // ticket zero for the next launch
           }
           if (++acc == Plan::kNumAcc) {
             acc = 0;
@@ -891,7 +896,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             if (lane == 0) release_acc(0);
           }
         }
-        if (partial && ticket_thread) p.counters[tile] = 0u;  // ticket zero for the next launch
+        if (partial && ticket_thread) p.counters[slot_tile] = 0u;  // ticket zero for the next launch
       }
       tc_fence_before();
       __syncwarp();

@@ -19,7 +19,7 @@ tile_n       tile columns: one MMA N <= 256, or 512 for a CTA pair (two MMAs
 tile_k       K per pipeline stage: 64 (one 128-byte swizzle row of fp16)
 stages       depth of the TMA -> shared-memory ring
 mma_sm       SMs that cooperate on one MMA: 1, or 2 (a CTA pair issuing
-             tcgen05 cta_group::2; no split-K)
+             tcgen05 cta_group::2; no split-K, stream-K for tile_n <= 256)
 raster       tile walk order: 0 = M fastest inside groups of tile-rows,
              1 = N fastest inside groups of tile-columns
 group        width of those groups (L2 reuse between concurrent CTAs)
@@ -123,7 +123,9 @@ def valid(cfg: Sequence[int]) -> bool:
         return False
     if smem_bytes(tile_m, tile_n, tile_k, stages, mma_sm) > SMEM_CAP:
         return False
-    if mma_sm == 2 and split_k != 1:
+    # CTA pairs: no data-parallel split-K; stream-K for the double-buffered
+    # 128- and 256-column pair tiles (each CTA reduces its own 128 rows)
+    if mma_sm == 2 and not (split_k == 1 or (split_k == 0 and tile_n <= 256)):
         return False
     if tmem_cols(tile_n) > TMEM_COLS:
         return False

@@ -90,6 +90,22 @@ def test_stream_k(cuda_device, M, N, K, tile_n):
     _check(M, N, K, _cfg(tile_n, 4, 0, 8, 0), dist="skinny", seed=M + N + K)
 
 
+@pytest.mark.parametrize("M,N,K,tile_n", [(320, 704, 328, 128), (1100, 1536, 2048, 256), (100, 1000, 4096, 256),
+                                           (130, 3000, 1000, 128), (2048, 2048, 2048, 256), (4096, 1024, 4096, 256)])
+def test_stream_k_pairs(cuda_device, M, N, K, tile_n):
+    """Stream-K on CTA pairs: each CTA of the pair reduces its own 128 rows (M=100: the odd CTA has none)."""
+    _check(M, N, K, _cfg(tile_n, 4, 0, 8, 0, mma_sm=2), dist="skinny", seed=M + K)
+
+
+def test_stream_k_pairs_large_sampled_rows(cuda_device):
+    """4096^3 on stream-K pairs (256 tiles on 74 pairs: every tile split), oracle on sampled rows."""
+    n = 4096
+    A, B = make_inputs(n, n, n, seed=7)
+    C = capi_gemm(A.cuda(), B.cuda(), _cfg(256, 4, 1, 8, 0, mma_sm=2))
+    rows = np.concatenate([np.random.default_rng(1).choice(n, size=40, replace=False), [0, 255, 256, n - 1]])
+    assert_close(C[torch.as_tensor(rows, device=C.device)], oracle_gemm(A[rows], B), n, "4096^3 stream-K pairs")
+
+
 def test_split_k_clamped_to_k_blocks(cuda_device):
     # K=100 has 2 K blocks; split 16 is clamped to 2
     _check(64, 512, 100, _cfg(128, 4, 0, 8, 16))

@@ -23,7 +23,8 @@ def test_valid_rules():
     assert not gen.valid((128, 128, 64, 4, 1, 0, 0, 1))   # group >= 1
     assert gen.valid((128, 128, 64, 4, 1, 0, 8, 0))       # split_k = 0: stream-K
     assert not gen.valid((128, 128, 64, 4, 1, 0, 8, -1))
-    assert not gen.valid((256, 256, 64, 4, 2, 0, 8, 0))   # no stream-K for CTA pairs
+    assert gen.valid((256, 256, 64, 4, 2, 0, 8, 0))       # stream-K for double-buffered pair tiles
+    assert not gen.valid((256, 512, 64, 4, 2, 0, 8, 0))   # ... not for the single-accumulator 512 tile
 
 
 def test_every_valid_combination_is_in_the_menu():
@@ -45,7 +46,8 @@ def test_smem_fits_and_max_stages_per_tile():
 
 def test_pair_rules():
     assert gen.valid((256, 256, 64, 6, 2, 0, 8, 1))
-    assert not gen.valid((256, 256, 64, 6, 2, 0, 8, 2))   # no split-K for CTA pairs
+    assert not gen.valid((256, 256, 64, 6, 2, 0, 8, 2))   # no data-parallel split-K for CTA pairs
+    assert gen.valid((256, 128, 64, 8, 2, 1, 4, 0))       # stream-K pairs
     assert not gen.valid((256, 192, 64, 4, 2, 0, 8, 1))   # 96 columns per CTA is not a 64-column atom
     assert not gen.valid((256, 64, 64, 4, 2, 0, 8, 1))
     assert not gen.valid((256, 256, 64, 7, 2, 0, 8, 1))   # shared memory
