@@ -200,6 +200,8 @@ struct Plan {
   int tiles_m = 0, tiles_n = 0, num_tiles = 0, kb_total = 0;
   bool streamk = false;
   int workers = 0;    // persistent CTAs (CTA pairs for cg = 2)
+  int dp_tiles = 0;   // stream-K: tiles walked data-parallel first
+  int64_t sk_iters = 0;  // stream-K: iterations of the stream-K region
   int max_parts = 1;  // partial slots per tile
   bool pack_a = false, pack_b = false;
   size_t off_partials = 0, off_pack_a = 0, off_pack_b = 0, total = 0;
@@ -282,11 +284,17 @@ int make_plan(const void* A, const void* B, int64_t M, int64_t N, int64_t K, int
   pl->workers = static_cast<int>(units < slots ? units : slots);
   pl->max_parts = pl->split_k;
   if (pl->streamk) {
-    const int64_t T = static_cast<int64_t>(pl->num_tiles) * pl->kb_total;
-    pl->workers = static_cast<int>(T < slots ? T : slots);
+    // Hybrid stream-K: all full waves but the last run data-parallel; the
+    // remaining 1-2 waves' worth of tiles are split evenly by iterations.
+    const int64_t T_all = static_cast<int64_t>(pl->num_tiles) * pl->kb_total;
+    pl->workers = static_cast<int>(T_all < slots ? T_all : slots);
+    const int64_t full_waves = pl->num_tiles / pl->workers;
+    pl->dp_tiles = static_cast<int>(full_waves > 1 ? (full_waves - 1) * pl->workers : 0);
+    const int64_t T = static_cast<int64_t>(pl->num_tiles - pl->dp_tiles) * pl->kb_total;
+    pl->sk_iters = T;
     int64_t mp = 1;
-    for (int64_t tile = 0; tile < pl->num_tiles; ++tile) {
-      const int64_t t0 = tile * pl->kb_total;
+    for (int64_t tile = pl->dp_tiles; tile < pl->num_tiles; ++tile) {
+      const int64_t t0 = (tile - pl->dp_tiles) * pl->kb_total;
       const int64_t parts = sk_owner(t0 + pl->kb_total - 1, T, pl->workers) - sk_owner(t0, T, pl->workers) + 1;
       if (parts > mp) mp = parts;
     }
@@ -585,7 +593,8 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
   p.kb_total = pl.kb_total;
   p.streamk = pl.streamk ? 1 : 0;
   p.max_parts = pl.max_parts;
-  p.total_iters = static_cast<long long>(pl.num_tiles) * pl.kb_total;
+  p.dp_tiles = pl.dp_tiles;
+  p.total_iters = pl.streamk ? pl.sk_iters : static_cast<long long>(pl.num_tiles) * pl.kb_total;
   p.raster = pl.raster;
   p.group = pl.group;
   p.c_tma = c_tma ? 1 : 0;

@@ -58,9 +58,10 @@ struct GemmParams {
   int num_tiles;
   int split_k;    // >= 1, <= kb_total (1 when CG = 2); 1 in stream-K mode
   int kb_total;   // ceil(K / kBK)
-  int streamk;    // 1: stream-K (CG = 1 only), each worker owns an equal share of all (tile, K-block) iterations
+  int streamk;    // 1: stream-K: tiles [0, dp_tiles) data-parallel, the rest split evenly by iterations
+  int dp_tiles;   // stream-K: whole tiles walked data-parallel before the stream-K region
   int max_parts;  // partial slots per tile in the workspace (split_k, or the most stream-K pieces of any tile)
-  long long total_iters;  // num_tiles * kb_total
+  long long total_iters;  // stream-K: (num_tiles - dp_tiles) * kb_total iterations of the stream-K region
   int raster;     // 0: groups of `group` tile-rows, M fastest; 1: groups of tile-columns, N fastest
   int group;      // >= 1
   int c_tma;      // 1: TMA-store epilogue; 0: coalesced st.global epilogue (any pitch)
@@ -161,21 +162,29 @@ struct Unit {
 //    advance through their units in lock-step waves, and every other wave
 //    walks K from the end (serpentine order): consecutive waves share operand
 //    blocks, and the K slices a wave touched last are the ones still in L2.
-//  * stream-K: the worker owns iterations [worker*T/W, (worker+1)*T/W) of the
-//    T = num_tiles * kb_total (tile, K-block) iterations, cut at tile
-//    boundaries, so every SM gets the same amount of MMA work whatever the
-//    tile count.
+//  * stream-K (hybrid): the first dp_tiles tiles are walked data-parallel as
+//    above, whole tiles in waves; the last one to two waves' worth of tiles
+//    form the stream-K region, whose T = (num_tiles - dp_tiles) * kb_total
+//    (tile, K-block) iterations are split evenly, worker w owning
+//    [w*T/W, (w+1)*T/W) cut at tile boundaries.  No SM idles in a partial
+//    last wave, and the concurrent tiles stay neighbours in the raster order
+//    (an all-stream-K walk spreads the workers over the whole tile range at
+//    once and loses L2 reuse).
 struct WorkIter {
-  long long cur, end;
+  long long cur, end;  // stream-K region / data-parallel unit index and limit
+  int dp;              // stream-K mode: next data-parallel tile of this worker
   int count;
 };
 
 __device__ __forceinline__ WorkIter work_begin(const GemmParams& p, int worker, int workers) {
   WorkIter w;
   if (p.streamk) {
-    w.cur = static_cast<long long>(worker) * p.total_iters / workers;
-    w.end = static_cast<long long>(worker + 1) * p.total_iters / workers;
+    const long long base = static_cast<long long>(p.dp_tiles) * p.kb_total;
+    w.dp = worker;
+    w.cur = base + static_cast<long long>(worker) * p.total_iters / workers;
+    w.end = base + static_cast<long long>(worker + 1) * p.total_iters / workers;
   } else {
+    w.dp = 0;
     w.cur = worker;
     w.end = static_cast<long long>(p.num_tiles) * p.split_k;
   }
@@ -183,21 +192,32 @@ __device__ __forceinline__ WorkIter work_begin(const GemmParams& p, int worker, 
   return w;
 }
 
-// Worker that owns stream-K iteration x.
+// Worker that owns iteration x of the stream-K region (x counted from the
+// region's start).
 __device__ __forceinline__ int sk_owner(const GemmParams& p, long long x, int workers) {
   return static_cast<int>(((x + 1) * workers - 1) / p.total_iters);
 }
 
 __device__ __forceinline__ bool work_next(const GemmParams& p, int worker, int workers, WorkIter& it, Unit& w) {
-  if (it.cur >= it.end) return false;
   const int kbt = p.kb_total;
-  if (p.streamk) {
+  if (p.streamk && it.dp < p.dp_tiles) {
+    // data-parallel part of a stream-K walk: one whole tile per unit
+    w.tile = it.dp;
+    w.kb0 = 0;
+    w.kb1 = kbt;
+    w.part = 0;
+    w.nparts = 1;
+    w.down = (it.count & 1) != 0;
+    it.dp += workers;
+  } else if (it.cur >= it.end) {
+    return false;
+  } else if (p.streamk) {
     w.tile = static_cast<int>(it.cur / kbt);
     w.kb0 = static_cast<int>(it.cur - static_cast<long long>(w.tile) * kbt);
     const long long left = it.end - it.cur;
     w.kb1 = (left < kbt - w.kb0) ? w.kb0 + static_cast<int>(left) : kbt;
     it.cur += w.kb1 - w.kb0;
-    const long long t0 = static_cast<long long>(w.tile) * kbt;
+    const long long t0 = static_cast<long long>(w.tile - p.dp_tiles) * kbt;
     const int first = sk_owner(p, t0, workers);
     w.part = worker - first;
     w.nparts = sk_owner(p, t0 + kbt - 1, workers) - first + 1;
