@@ -30,25 +30,24 @@ cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtens
     if (e != cudaSuccess) return e;
     configured.fetch_or(bit, std::memory_order_acq_rel);
   }
-  if constexpr (CG == 1) {
-    kernel<<<grid, kNumThreads, Plan::kDynamicBytes, stream>>>(a, b, c, p);
-    return cudaGetLastError();
-  } else {
-    // CTA pairs: a cluster of 2 along x; grid is a multiple of 2.
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
-    cfg.blockDim = dim3(kNumThreads, 1, 1);
-    cfg.dynamicSmemBytes = Plan::kDynamicBytes;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kernel, a, b, c, p);
-  }
+  // Programmatic dependent launch: the kernel's set-up may overlap the end
+  // of the previous grid in the stream (it waits with griddepcontrol.wait
+  // before touching global memory).  CTA pairs: a cluster of 2 along x.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(kNumThreads, 1, 1);
+  cfg.dynamicSmemBytes = Plan::kDynamicBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 2;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = CG == 2 ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, kernel, a, b, c, p);
 }
 
 }  // namespace idb

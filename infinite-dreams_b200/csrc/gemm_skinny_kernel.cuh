@@ -104,6 +104,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();  // global memory only after the previous grid in the stream has completed
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -140,6 +141,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           phase ^= 1u;
         }
       }
+      griddep_launch_dependents();  // every load of this CTA is issued
       if (!ok) {
         *abort_flag = 1;
         atomicOr(p.err, kDevErrTimeoutProducer);
@@ -310,13 +312,15 @@ cudaError_t launch_skinny(const CUtensorMap& a, const CUtensorMap& b, const Gemm
   cfg.blockDim = dim3(kNumThreads, 1, 1);
   cfg.dynamicSmemBytes = Plan::kDynamicBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = static_cast<unsigned>(cluster);
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see griddep_wait()
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, kernel, a, b, p);
 }
 

@@ -531,6 +531,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   if constexpr (CG == 2) cluster_sync();   // the peer's barriers are initialised before any remote use
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // The set-up above touches no global memory, so it may overlap the tail of
+  // the previous grid in the stream (programmatic dependent launch); every
+  // global access below comes after that grid has completed.
+  griddep_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -596,6 +600,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           }
         }
       }
+      // every load of this CTA is issued: the next grid may begin its set-up
+      griddep_launch_dependents();
       if (!ok) {
         *abort_flag = 1;
         atomicOr(p.err, kDevErrTimeoutProducer);

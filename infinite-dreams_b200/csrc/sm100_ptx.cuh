@@ -101,6 +101,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   return mbar_wait_limit(bar, parity, abort_flag, kWaitLimitNs);
 }
 
+// ----------------------------------------------------------------- programmatic dependent launch
+// A grid launched with programmatic stream serialization may start while the
+// previous grid in the stream is still running; griddep_wait() returns once
+// that grid has completed and its memory is visible, so everything that reads
+// or writes global memory comes after it.  griddep_launch_dependents() lets
+// the next such grid begin its own set-up early.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ----------------------------------------------------------------- clusters
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
