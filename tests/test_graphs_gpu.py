@@ -87,3 +87,42 @@ def test_graph_timing_mode(cuda_device):
     cid = ext.default_cfg(256, 256, 256)
     ms = time_cuda_ms(lambda: ext.gemm_forward_cfg(Ad, Bd, cid, out=out), iters=20, warmup=3, graph=True)
     assert 0.0005 < ms < 0.05, ms      # back-to-back device time of a 256^3 GEMM, in ms
+
+
+@pytest.mark.parametrize("shape,knobs", [
+    ((512, 512, 512), (128, 64, 64, 6, 1, 1, 2, 1)),       # main kernel, 1 CTA
+    ((1024, 1024, 1024), (256, 256, 64, 4, 2, 0, 8, 1)),   # CTA pairs
+    ((16, 1000, 1000), (16, 128, 64, 8, 1, 0, 1, 4)),      # skinny kernel, cluster split-K
+    ((300, 777, 777), (128, 128, 64, 4, 1, 0, 8, 4)),      # unaligned pitch: pack kernel + split-K
+])
+def test_chained_launches_see_the_previous_result(cuda_device, shape, knobs):
+    """x_{i+1} = x_i @ W on one stream with no sync in between: each launch may start its set-up under the
+    previous grid (programmatic dependent launch) but must read that grid's output.  Compared bit for bit
+    with the same chain synchronised after every step."""
+    from infinite_dreams import infinite_dreams_ext as ext
+    M, N, K = shape
+    assert N == K
+    cid = _cfg(knobs)
+    g = torch.Generator().manual_seed(5)
+    W = ((torch.rand((K, N), generator=g) * 2 - 1) / (K ** 0.5)).half().cuda()
+    x0 = (torch.rand((M, K), generator=g) * 2 - 1).half().cuda()
+    outs = [torch.empty((M, N), dtype=torch.float16, device="cuda") for _ in range(8)]
+
+    def chain(sync):
+        x = x0
+        for o in outs:
+            ext.gemm_forward_cfg(x, W, cid, out=o)
+            if sync:
+                torch.cuda.synchronize()
+            x = o
+        torch.cuda.synchronize()
+        return [o.clone() for o in outs]
+
+    ref = chain(sync=True)
+    for o in outs:
+        o.fill_(float("nan"))
+    got = chain(sync=False)
+    for i, (a, b) in enumerate(zip(got, ref)):
+        assert torch.isfinite(a.float()).all(), i
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16)), (shape, i)
+    ext.check_device_errors()
