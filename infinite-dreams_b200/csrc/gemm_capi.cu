@@ -68,6 +68,10 @@ static const SkinnyVariant kSkinnyVariants[] = {
 // caller's A or B pitch / base address is not 16-byte aligned.
 __global__ void pack_rows_f16(const __half* __restrict__ src, long long lds, __half* __restrict__ dst,
                               long long ldd, int rows, int cols) {
+  // The GEMM that reads the packed copy is launched as a programmatic
+  // dependent: let it start its set-up now (it waits for this grid's
+  // completion before it reads anything).
+  griddep_launch_dependents();
   const long long chunks = (cols + 7) / 8;
   const long long total = static_cast<long long>(rows) * chunks;
   const unsigned short* s16 = reinterpret_cast<const unsigned short*>(src);
