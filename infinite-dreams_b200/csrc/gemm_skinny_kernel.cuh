@@ -12,11 +12,14 @@
 //    [64 K x TN] tile of B (16 or 32 KiB, all useful) and a [TM x 64 K]
 //    tile of A (2-8 KiB), so the ring holds ~200 KiB of B in flight;
 //  * split-K inside a thread-block cluster: the S CTAs of a cluster own the
-//    same 128 columns and S consecutive K ranges.  Each writes its fp32
-//    partial tile into its own (now idle) pipeline buffers; after a cluster
-//    barrier, CTA r sums columns [r*TN/S, (r+1)*TN/S) of all S partials
-//    through distributed shared memory, in rank order (deterministic), and
-//    stores C.  No workspace, no atomics, no second pass over global memory.
+//    same TN columns and S consecutive K ranges.  CTA r owns columns
+//    [r*TN/S, (r+1)*TN/S) of the block.  After a cluster barrier (every
+//    pipeline drained), each CTA stores its fp32 accumulator values straight
+//    from TMEM into the owner's idle pipeline buffers through distributed
+//    shared memory (posted stores, one slot per sender); after a second
+//    barrier each owner sums its S slots in rank order (deterministic) from
+//    its own shared memory and stores C.  No workspace, no atomics, no
+//    second pass over global memory, no remote loads.
 //
 // Roles as in gemm_sm100_kernel.cuh: warp 0 TMA producer, warp 1 TMEM owner
 // and MMA issuer, warps 2..5 read the accumulator.  Every mbarrier wait is
@@ -49,11 +52,11 @@ struct SkinnyPlan {
   static constexpr int kDynamicBytes = kUsed + 1024;
   static constexpr uint32_t kTmemCols =
       kNB * TM <= 32 ? 32 : (kNB * TM <= 64 ? 64 : (kNB * TM <= 128 ? 128 : 256));
-  static constexpr int kPartialBytes = TM * TN * 4;  // fp32 [TM][TN]
+  static constexpr int kPartialBytes = TM * TN * 4;  // receive buffer fp32 [S][TM][TN / S]
   static_assert(TM == 16 || TM == 32 || TM == 64, "MMA N of the swapped tile");
   static_assert(TN == 128 || TN == 256 || TN == 512, "one, two or four 128-row MMAs");
   static_assert(kMBytes % 1024 == 0, "swizzled A tiles need 1024-byte alignment");
-  static_assert(kPartialBytes <= kOffBar, "the partial tile reuses the pipeline buffers");
+  static_assert(kPartialBytes <= kOffBar, "the receive buffer reuses the pipeline buffers");
 };
 
 template <int TM, int TN, int STAGES>
@@ -70,7 +73,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   uint64_t* tfull_bar = empty_bar + STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Plan::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* partial = reinterpret_cast<float*>(smem);  // after the mainloop: fp32 [TM][TN]
+  float* recv = reinterpret_cast<float*>(smem);  // after the mainloop: fp32 [S][TM][TN / S]
 
   const int warp = static_cast<int>(threadIdx.x >> 5);
   const int lane = static_cast<int>(threadIdx.x & 31);
@@ -105,6 +108,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   griddep_wait();  // global memory only after the previous grid in the stream has completed
+  bool acc_ok = true;  // epilogue warps: the accumulator barrier completed in time
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -197,7 +201,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         atomicOr(p.err, kDevErrTimeoutMma);
       }
       // tfull completes when every MMA above has retired (also what makes
-      // the pipeline buffers free for the partial tile and TMEM safe to free)
+      // the pipeline buffers free to receive partial tiles and TMEM safe to free)
       mma_commit<1>(tfull_bar);
       const uint64_t t0 = globaltimer_ns();
       while (!mbar_try_wait(tfull_bar, 0)) {
@@ -208,59 +212,75 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------ accumulator -> partial tile
-    const int ew = warp & 3;
-    const int n_local = ew * 32 + lane;
+    // ------------------------------------------------------------ wait for the accumulator
     // One lane per warp polls the barrier through the whole mainloop; the
     // others wait at the shuffle instead of competing for issue slots with
     // the producer and MMA threads.
     bool got = true;
     if (lane == 0) got = mbar_wait(tfull_bar, 0, abort_flag);
     got = __shfl_sync(0xffffffffu, got ? 1 : 0, 0) != 0;
-    const bool ok = named_bar_and(1, 32 * kEpiWarps, got);
-    tc_fence_after();
-    if (ok) {
-      // accumulator h holds columns [h*TM, (h+1)*TM) of TMEM: rows m of C for
-      // the columns n0 + h*128 + lane row
-#pragma unroll
-      for (int c32 = 0; c32 < (Plan::kNB * TM + 31) / 32; ++c32) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + c32 * 32, v);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int col = c32 * 32 + i;
-          if (col < Plan::kNB * TM) {
-            const int h = col / TM, m = col - h * TM;
-            partial[m * TN + h * kSkinnyN + n_local] = __uint_as_float(v[i]);
-          }
-        }
-      }
-    } else {
+    acc_ok = named_bar_and(1, 32 * kEpiWarps, got);
+    if (!acc_ok && threadIdx.x == 64) {
       *abort_flag = 1;
       atomicOr(p.err, kDevErrTimeoutEpilogue);
     }
   }
 
   // ------------------------------------------------------------ cluster reduction
+  // Barrier 1: every CTA of the cluster has drained its pipeline (all fills
+  // landed, all MMAs retired), so its buffers may now receive partial tiles.
   tc_fence_before();
   __syncwarp();
-  cluster_sync();  // every CTA's partial tile is written and visible in the cluster
+  cluster_sync();
+  tc_fence_after();
+  const int ns = TN / S;  // columns of the block this CTA reduces and stores
+  if (warp >= 2 && acc_ok) {
+    // Push: each accumulator value goes straight from TMEM to the CTA that
+    // owns its column, into slot `rank` of that CTA's receive buffer
+    // fp32 [S][TM][ns].  The stores are posted (no round trip), and each
+    // warp instruction writes 128 contiguous bytes.
+    const int ew = warp & 3;
+    const int n_local = ew * 32 + lane;
+    const uint32_t base = smem_u32(recv);
+#pragma unroll
+    for (int c32 = 0; c32 < (Plan::kNB * TM + 31) / 32; ++c32) {
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + c32 * 32, v);
+      tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int col = c32 * 32 + i;
+        if (col < Plan::kNB * TM) {
+          // accumulator h holds TMEM columns [h*TM, (h+1)*TM): rows m of C
+          // for column h*128 + n_local of the block
+          const int h = col / TM, m = col - h * TM;
+          const int bcol = h * kSkinnyN + n_local;
+          const int owner = bcol / ns;
+          const uint32_t off = static_cast<uint32_t>(((rank * TM + m) * ns + bcol - owner * ns) * 4);
+          st_dsmem_f32(mapa_shared(base + off, static_cast<uint32_t>(owner)), __uint_as_float(v[i]));
+        }
+      }
+    }
+  }
+  // Barrier 2: every partial has reached its owner (release/acquire at
+  // cluster scope); from here each CTA reads only its own shared memory, so
+  // no CTA waits for another one before leaving.
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync();
   {
-    const int ns = TN / S;             // columns this CTA reduces
-    const int g_per_row = ns / 4;      // 4-column groups per row
+    const int g_per_row = ns / 4;  // 4-column groups per row
     const int groups = TM * g_per_row;
-    const uint32_t base = smem_u32(partial);
     const bool vec = ((reinterpret_cast<uintptr_t>(p.C) | static_cast<uintptr_t>(p.ldc * 2)) & 7u) == 0;
     for (int g = static_cast<int>(threadIdx.x); g < groups; g += kNumThreads) {
       const int m = g / g_per_row;
-      const int n = rank * ns + (g - m * g_per_row) * 4;
-      const int gm = m0 + m, gn = n0 + n;
+      const int n = (g - m * g_per_row) * 4;
+      const int gm = m0 + m, gn = n0 + rank * ns + n;
       if (gm >= p.M || gn >= p.N) continue;
-      const uint32_t off = static_cast<uint32_t>((m * TN + n) * 4);
-      float4 acc = ld_dsmem_f4(mapa_shared(base + off, 0));
+      // sum the S slots in rank order: the same result whatever the timing
+      float4 acc = *reinterpret_cast<const float4*>(recv + m * ns + n);
       for (int q = 1; q < S; ++q) {
-        const float4 x = ld_dsmem_f4(mapa_shared(base + off, static_cast<uint32_t>(q)));
+        const float4 x = *reinterpret_cast<const float4*>(recv + (q * TM + m) * ns + n);
         acc.x += x.x;
         acc.y += x.y;
         acc.z += x.z;
@@ -285,7 +305,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       }
     }
   }
-  cluster_sync();  // no CTA leaves while a peer may still read its partial tile
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc<1>(tmem_base, Plan::kTmemCols);
