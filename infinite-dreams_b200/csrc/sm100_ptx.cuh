@@ -139,17 +139,6 @@ __device__ __forceinline__ uint32_t cluster_id_x() {
   return r;
 }
 
-// 16-byte load from shared memory of a CTA in the cluster (distributed
-// shared memory), given a shared::cluster address from mapa_shared.
-__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t cluster_addr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(cluster_addr)
-               : "memory");
-  return v;
-}
-
 // 4-byte store into shared memory of a CTA in the cluster (posted: the
 // thread does not wait for it; a cluster barrier with release/acquire
 // semantics makes it visible to the owner).
