@@ -45,8 +45,8 @@ static const Variant kVariants[] = {
 
 #define IDB_SKINNY(TM, TN, ST)                                                                           \
   cudaError_t launch_skinny_tm##TM##_tn##TN##_s##ST(const CUtensorMap& a, const CUtensorMap& b,           \
-                                                    const GemmParams& p, int grid, int cluster,           \
-                                                    cudaStream_t stream);
+                                                    const CUtensorMap& c, const GemmParams& p, int grid,  \
+                                                    int cluster, cudaStream_t stream);
 #include "generated/gemm_skinny_variants.inc"
 #undef IDB_SKINNY
 
@@ -335,8 +335,10 @@ int make_plan(const void* A, const void* B, int64_t M, int64_t N, int64_t K, int
   return GEMM_OK;
 }
 
+// swizzled = true: 128-byte swizzle (operand tiles and the main kernel's C
+// boxes); false: plain row-major boxes (the skinny kernel's C blocks).
 int encode_2d(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, int64_t pitch_elems, int box_inner,
-              int box_outer, const char* what) {
+              int box_outer, const char* what, bool swizzled = true) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(GEMM_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
@@ -344,7 +346,8 @@ int encode_2d(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, 
   const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_outer)};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzled ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     return fail(GEMM_ERR_CUDA, std::string("cuTensorMapEncodeTiled(") + what + ") failed with CUresult " +
@@ -354,13 +357,14 @@ int encode_2d(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, 
 }
 
 // Recently encoded tensor maps of the calling thread.  A map depends only on
-// the address, extents, pitch and box, so repeated launches on the same
+// the address, extents, pitch, box and swizzle, so repeated launches on the same
 // buffers (the common case: a tuner loop, a model step) reuse it instead of
 // encoding it again.
 struct MapCacheEntry {
   const void* base = nullptr;
   int64_t inner = 0, outer = 0, pitch = 0;
   int box_inner = 0, box_outer = 0;
+  bool swizzled = true;
   bool valid = false;
   CUtensorMap map;
 };
@@ -369,15 +373,15 @@ thread_local MapCacheEntry t_map_cache[kMapCacheSize];
 thread_local int t_map_next = 0;
 
 int encode_2d_cached(CUtensorMap* map, const void* base, int64_t inner, int64_t outer, int64_t pitch_elems,
-                     int box_inner, int box_outer, const char* what) {
+                     int box_inner, int box_outer, const char* what, bool swizzled = true) {
   for (const MapCacheEntry& e : t_map_cache) {
     if (e.valid && e.base == base && e.inner == inner && e.outer == outer && e.pitch == pitch_elems &&
-        e.box_inner == box_inner && e.box_outer == box_outer) {
+        e.box_inner == box_inner && e.box_outer == box_outer && e.swizzled == swizzled) {
       *map = e.map;
       return GEMM_OK;
     }
   }
-  const int st = encode_2d(map, base, inner, outer, pitch_elems, box_inner, box_outer, what);
+  const int st = encode_2d(map, base, inner, outer, pitch_elems, box_inner, box_outer, what, swizzled);
   if (st != GEMM_OK) return st;
   MapCacheEntry& e = t_map_cache[t_map_next];
   t_map_next = (t_map_next + 1) % kMapCacheSize;
@@ -387,6 +391,7 @@ int encode_2d_cached(CUtensorMap* map, const void* base, int64_t inner, int64_t 
   e.pitch = pitch_elems;
   e.box_inner = box_inner;
   e.box_outer = box_outer;
+  e.swizzled = swizzled;
   e.map = *map;
   e.valid = true;
   return GEMM_OK;
@@ -549,7 +554,9 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
 
   if (pl.skinny) {
     // A: [tile_m rows x 64 K] boxes; B: [128 n x 64 K] (stored N x K) or
-    // [64 K x 64 n] atoms (stored K x N); C is written with plain stores.
+    // [64 K x 64 n] atoms (stored K x N); C: plain [min(tile_n / S, 256) x
+    // tile_m] boxes written by TMA stores when C is TMA-addressable, else
+    // per-thread stores.
     st = encode_2d_cached(&tmA, a_src, K, M, a_ld, kBK, pl.tile_m, "A");
     if (st != GEMM_OK) return st;
     if (op.trans_b) {
@@ -565,7 +572,13 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
     p.split_k = pl.split_k;
     p.partials = nullptr;
     p.counters = nullptr;
-    e = svar->fn(tmA, tmB, p, pl.num_tiles * pl.split_k, pl.split_k, stream);
+    const bool c_tma = tma_addressable(C, ldc);
+    if (c_tma) {
+      st = encode_2d_cached(&tmC, C, N, M, ldc, skinny_c_box(pl.tile_n / pl.split_k), pl.tile_m, "C", false);
+      if (st != GEMM_OK) return st;
+    }
+    p.c_tma = c_tma ? 1 : 0;
+    e = svar->fn(tmA, tmB, tmC, p, pl.num_tiles * pl.split_k, pl.split_k, stream);
     if (e != cudaSuccess) return fail_cuda(e, "skinny gemm kernel launch");
     return GEMM_OK;
   }

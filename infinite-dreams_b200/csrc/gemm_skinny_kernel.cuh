@@ -57,12 +57,23 @@ struct SkinnyPlan {
   static_assert(TN == 128 || TN == 256 || TN == 512, "one, two or four 128-row MMAs");
   static_assert(kMBytes % 1024 == 0, "swizzled A tiles need 1024-byte alignment");
   static_assert(kPartialBytes <= kOffBar, "the receive buffer reuses the pipeline buffers");
+  // fp16 staging of the finished C block for its TMA store: [TM][TN] at
+  // offset 0 for a cluster of one; [TM][TN / S] after the receive buffer
+  // otherwise (S >= 2)
+  static constexpr int kStageCOff = kPartialBytes;
+  static_assert(TM * TN * 2 <= kOffBar, "C staging of a cluster of one reuses the pipeline buffers");
+  static_assert(kStageCOff + TM * (TN / 2) * 2 <= kOffBar, "C staging after the receive buffer");
 };
+
+// Width of one TMA store box of C (columns): a block of `ns` columns is
+// stored as ns / box boxes of [TM rows x box columns], staged one after the
+// other, each row-major.  The tensor map's box is [min(ns, 256) x TM].
+__host__ __device__ constexpr int skinny_c_box(int ns) { return ns < 256 ? ns : 256; }
 
 template <int TM, int TN, int STAGES>
 __global__ void __launch_bounds__(kNumThreads, 1)
     gemm_skinny_f16(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const GemmParams p) {
+                    const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
   using Plan = SkinnyPlan<TM, TN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -98,6 +109,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    if (p.c_tma) prefetch_tmap(&tmC);
   }
   if (warp == 1) {
     tmem_alloc<1>(tmem_slot, Plan::kTmemCols);
@@ -226,82 +238,160 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     }
   }
 
-  // ------------------------------------------------------------ cluster reduction
-  // Barrier 1: every CTA of the cluster has drained its pipeline (all fills
-  // landed, all MMAs retired), so its buffers may now receive partial tiles.
-  tc_fence_before();
-  __syncwarp();
-  cluster_sync();
-  tc_fence_after();
-  const int ns = TN / S;  // columns of the block this CTA reduces and stores
-  if (warp >= 2 && acc_ok) {
-    // Push: each accumulator value goes straight from TMEM to the CTA that
-    // owns its column, into slot `rank` of that CTA's receive buffer
-    // fp32 [S][TM][ns].  The stores are posted (no round trip), and each
-    // warp instruction writes 128 contiguous bytes.
-    const int ew = warp & 3;
-    const int n_local = ew * 32 + lane;
-    const uint32_t base = smem_u32(recv);
+  // Per-thread global stores issued at the very end of a launch are slow
+  // (each waits behind the memory traffic of the CTAs still streaming), so
+  // when C is TMA-addressable the finished block is staged in shared memory
+  // as fp16 and written by one TMA store per box.
+  if (S == 1 && p.c_tma) {
+    // ------------------------------------------------------------ one CTA owns the block
+    // No partial tiles to combine and no peer: the pipeline buffers are free
+    // once this CTA's accumulator is complete (every fill was consumed by an
+    // MMA that has retired), so the epilogue warps stage C there directly.
+    constexpr int kBox = skinny_c_box(TN);
+    __half* stage = reinterpret_cast<__half*>(smem);
+    if (warp >= 2 && acc_ok) {
+      const int ew = warp & 3;
+      const int n_local = ew * 32 + lane;
 #pragma unroll
-    for (int c32 = 0; c32 < (Plan::kNB * TM + 31) / 32; ++c32) {
-      uint32_t v[32];
-      tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + c32 * 32, v);
-      tmem_ld_wait();
+      for (int c32 = 0; c32 < (Plan::kNB * TM + 31) / 32; ++c32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + c32 * 32, v);
+        tmem_ld_wait();
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int col = c32 * 32 + i;
-        if (col < Plan::kNB * TM) {
-          // accumulator h holds TMEM columns [h*TM, (h+1)*TM): rows m of C
-          // for column h*128 + n_local of the block
-          const int h = col / TM, m = col - h * TM;
-          const int bcol = h * kSkinnyN + n_local;
-          const int owner = bcol / ns;
-          const uint32_t off = static_cast<uint32_t>(((rank * TM + m) * ns + bcol - owner * ns) * 4);
-          st_dsmem_f32(mapa_shared(base + off, static_cast<uint32_t>(owner)), __uint_as_float(v[i]));
+        for (int i = 0; i < 32; ++i) {
+          const int col = c32 * 32 + i;
+          if (col < Plan::kNB * TM) {
+            // accumulator h holds TMEM columns [h*TM, (h+1)*TM): row m of C
+            // for column h*128 + n_local of the block
+            const int h = col / TM, m = col - h * TM;
+            const int bcol = h * kSkinnyN + n_local;
+            float x = __uint_as_float(v[i]);
+            if (p.epi) {
+              const int gm = m0 + m, gn = n0 + bcol;
+              float d = 0.0f, b = 0.0f;
+              if (gm < p.M && gn < p.N) {
+                if (p.beta != 0.0f) d = __half2float(p.D[static_cast<long long>(gm) * p.ldd + gn]);
+                if (p.bias != nullptr) b = __half2float(p.bias[gn]);
+              }
+              x = epilogue_value(p, x, d, b);
+            }
+            stage[(bcol / kBox) * (TM * kBox) + m * kBox + bcol % kBox] = __float2half_rn(x);
+          }
+        }
+      }
+      fence_proxy_async_smem();
+    }
+    tc_fence_before();
+    __syncwarp();
+    __syncthreads();  // staging complete; every tcgen05.ld has completed
+    if (threadIdx.x == 64 && acc_ok) {
+#pragma unroll
+      for (int b = 0; b < TN / kBox; ++b) {
+        // TMA clips the rows and columns past M and N; a box that starts
+        // past the last column has nothing to write
+        if (n0 + b * kBox < p.N) tma_store_2d(&tmC, stage + b * (TM * kBox), n0 + b * kBox, m0);
+      }
+      bulk_commit_group();
+      bulk_wait_group_read<0>();  // shared memory stays valid until the TMA has read it
+    }
+  } else {
+    // ------------------------------------------------------------ cluster reduction
+    // Barrier 1: every CTA of the cluster has drained its pipeline (all fills
+    // landed, all MMAs retired), so its buffers may now receive partial tiles.
+    tc_fence_before();
+    __syncwarp();
+    cluster_sync();
+    tc_fence_after();
+    const int ns = TN / S;  // columns of the block this CTA reduces and stores
+    if (warp >= 2 && acc_ok) {
+      // Push: each accumulator value goes straight from TMEM to the CTA that
+      // owns its column, into slot `rank` of that CTA's receive buffer
+      // fp32 [S][TM][ns].  The stores are posted (no round trip), and each
+      // warp instruction writes 128 contiguous bytes.
+      const int ew = warp & 3;
+      const int n_local = ew * 32 + lane;
+      const uint32_t base = smem_u32(recv);
+  #pragma unroll
+      for (int c32 = 0; c32 < (Plan::kNB * TM + 31) / 32; ++c32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + c32 * 32, v);
+        tmem_ld_wait();
+  #pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int col = c32 * 32 + i;
+          if (col < Plan::kNB * TM) {
+            // accumulator h holds TMEM columns [h*TM, (h+1)*TM): rows m of C
+            // for column h*128 + n_local of the block
+            const int h = col / TM, m = col - h * TM;
+            const int bcol = h * kSkinnyN + n_local;
+            const int owner = bcol / ns;
+            const uint32_t off = static_cast<uint32_t>(((rank * TM + m) * ns + bcol - owner * ns) * 4);
+            st_dsmem_f32(mapa_shared(base + off, static_cast<uint32_t>(owner)), __uint_as_float(v[i]));
+          }
         }
       }
     }
-  }
-  // Barrier 2: every partial has reached its owner (release/acquire at
-  // cluster scope); from here each CTA reads only its own shared memory, so
-  // no CTA waits for another one before leaving.
-  tc_fence_before();
-  __syncwarp();
-  cluster_sync();
-  {
-    const int g_per_row = ns / 4;  // 4-column groups per row
-    const int groups = TM * g_per_row;
-    const bool vec = ((reinterpret_cast<uintptr_t>(p.C) | static_cast<uintptr_t>(p.ldc * 2)) & 7u) == 0;
-    for (int g = static_cast<int>(threadIdx.x); g < groups; g += kNumThreads) {
-      const int m = g / g_per_row;
-      const int n = (g - m * g_per_row) * 4;
-      const int gm = m0 + m, gn = n0 + rank * ns + n;
-      if (gm >= p.M || gn >= p.N) continue;
-      // sum the S slots in rank order: the same result whatever the timing
-      float4 acc = *reinterpret_cast<const float4*>(recv + m * ns + n);
-      for (int q = 1; q < S; ++q) {
-        const float4 x = *reinterpret_cast<const float4*>(recv + (q * TM + m) * ns + n);
-        acc.x += x.x;
-        acc.y += x.y;
-        acc.z += x.z;
-        acc.w += x.w;
-      }
-      float* v = &acc.x;
-      if (p.epi) {
-        for (int c = 0; c < 4 && gn + c < p.N; ++c) {
-          const float d = (p.beta != 0.0f) ? __half2float(p.D[static_cast<long long>(gm) * p.ldd + gn + c]) : 0.0f;
-          const float b = (p.bias != nullptr) ? __half2float(p.bias[gn + c]) : 0.0f;
-          v[c] = epilogue_value(p, v[c], d, b);
+    // Barrier 2: every partial has reached its owner (release/acquire at
+    // cluster scope); from here each CTA reads only its own shared memory, so
+    // no CTA waits for another one before leaving.
+    tc_fence_before();
+    __syncwarp();
+    cluster_sync();
+    {
+      const int g_per_row = ns / 4;  // 4-column groups per row
+      const int groups = TM * g_per_row;
+      const bool vec = ((reinterpret_cast<uintptr_t>(p.C) | static_cast<uintptr_t>(p.ldc * 2)) & 7u) == 0;
+      __half* stage_c = reinterpret_cast<__half*>(smem + Plan::kStageCOff);  // [TM][ns] when C takes TMA stores
+      for (int g = static_cast<int>(threadIdx.x); g < groups; g += kNumThreads) {
+        const int m = g / g_per_row;
+        const int n = (g - m * g_per_row) * 4;
+        const int gm = m0 + m, gn = n0 + rank * ns + n;
+        if (gm >= p.M || gn >= p.N) continue;
+        // sum the S slots in rank order: the same result whatever the timing
+        float4 acc = *reinterpret_cast<const float4*>(recv + m * ns + n);
+        for (int q = 1; q < S; ++q) {
+          const float4 x = *reinterpret_cast<const float4*>(recv + (q * TM + m) * ns + n);
+          acc.x += x.x;
+          acc.y += x.y;
+          acc.z += x.z;
+          acc.w += x.w;
+        }
+        float* v = &acc.x;
+        if (p.epi) {
+          for (int c = 0; c < 4 && gn + c < p.N; ++c) {
+            const float d = (p.beta != 0.0f) ? __half2float(p.D[static_cast<long long>(gm) * p.ldd + gn + c]) : 0.0f;
+            const float b = (p.bias != nullptr) ? __half2float(p.bias[gn + c]) : 0.0f;
+            v[c] = epilogue_value(p, v[c], d, b);
+          }
+        }
+        if (p.c_tma) {
+          uint2 hv;
+          hv.x = pack_half2(v[0], v[1]);
+          hv.y = pack_half2(v[2], v[3]);
+          *reinterpret_cast<uint2*>(stage_c + m * ns + n) = hv;
+          continue;
+        }
+        __half* dst = p.C + static_cast<long long>(gm) * p.ldc + gn;
+        if (vec && gn + 3 < p.N) {
+          uint2 hv;
+          hv.x = pack_half2(v[0], v[1]);
+          hv.y = pack_half2(v[2], v[3]);
+          *reinterpret_cast<uint2*>(dst) = hv;
+        } else {
+          for (int c = 0; c < 4 && gn + c < p.N; ++c) dst[c] = __float2half_rn(v[c]);
         }
       }
-      __half* dst = p.C + static_cast<long long>(gm) * p.ldc + gn;
-      if (vec && gn + 3 < p.N) {
-        uint2 hv;
-        hv.x = pack_half2(v[0], v[1]);
-        hv.y = pack_half2(v[2], v[3]);
-        *reinterpret_cast<uint2*>(dst) = hv;
-      } else {
-        for (int c = 0; c < 4 && gn + c < p.N; ++c) dst[c] = __float2half_rn(v[c]);
+      if (p.c_tma) {
+        // one box of [TM rows x ns columns]; TMA clips the rows and columns
+        // past M and N, and a box that starts past the last column is skipped
+        fence_proxy_async_smem();
+        __syncwarp();
+        __syncthreads();
+        if (threadIdx.x == 64 && n0 + rank * ns < p.N) {
+          tma_store_2d(&tmC, stage_c, n0 + rank * ns, m0);
+          bulk_commit_group();
+          bulk_wait_group_read<0>();  // shared memory stays valid until the TMA has read it
+        }
       }
     }
   }
@@ -312,8 +402,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
 }
 
 template <int TM, int TN, int STAGES>
-cudaError_t launch_skinny(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, int grid, int cluster,
-                          cudaStream_t stream) {
+cudaError_t launch_skinny(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c, const GemmParams& p,
+                          int grid, int cluster, cudaStream_t stream) {
   using Plan = SkinnyPlan<TM, TN, STAGES>;
   auto kernel = gemm_skinny_f16<TM, TN, STAGES>;
   static std::atomic<unsigned long long> configured{0};
@@ -340,17 +430,17 @@ cudaError_t launch_skinny(const CUtensorMap& a, const CUtensorMap& b, const Gemm
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, kernel, a, b, p);
+  return cudaLaunchKernelEx(&cfg, kernel, a, b, c, p);
 }
 
-using SkinnyLaunchFn = cudaError_t (*)(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, int grid,
-                                       int cluster, cudaStream_t stream);
+using SkinnyLaunchFn = cudaError_t (*)(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c,
+                                       const GemmParams& p, int grid, int cluster, cudaStream_t stream);
 
 }  // namespace idb
 
 #define IDB_DEFINE_SKINNY(TM, TN, ST)                                                                     \
   cudaError_t launch_skinny_tm##TM##_tn##TN##_s##ST(const CUtensorMap& a, const CUtensorMap& b,            \
-                                                    const GemmParams& p, int grid, int cluster,            \
-                                                    cudaStream_t stream) {                                 \
-    return launch_skinny<TM, TN, ST>(a, b, p, grid, cluster, stream);                                     \
+                                                    const CUtensorMap& c, const GemmParams& p, int grid,   \
+                                                    int cluster, cudaStream_t stream) {                    \
+    return launch_skinny<TM, TN, ST>(a, b, c, p, grid, cluster, stream);                                  \
   }

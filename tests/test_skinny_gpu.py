@@ -130,3 +130,24 @@ def test_skinny_deterministic(cuda_device):
     first = capi_gemm(Ad, Bd, cid)
     for _ in range(3):
         assert torch.equal(capi_gemm(Ad, Bd, cid).view(torch.int16), first.view(torch.int16))
+
+
+@pytest.mark.parametrize("tm,tn,stages,split", [(16, 128, 12, 1), (64, 128, 8, 1), (16, 512, 3, 1),
+                                                (16, 256, 6, 2), (32, 128, 8, 4), (16, 128, 12, 8)])
+def test_skinny_tma_store_matches_plain_stores(cuda_device, tm, tn, stages, split):
+    """A C whose base and pitch TMA can address takes TMA stores of the staged block; an odd pitch takes
+    per-thread stores.  Both give the oracle's result bit for bit, and neither writes outside its view
+    (ragged M and N: the TMA clips at the tensor map's extent)."""
+    M, N, K = tm + 5, 1000, 700
+    A, B = make_inputs(M, N, K, dist="skinny", seed=tm * tn + split)
+    ref = oracle.gemm_f16(A.numpy(), B.numpy())
+    Ad, Bd = A.cuda(), B.cuda()
+    cid = _cfg(tm, stages, split, tn)
+    big = torch.full((M + 3, N + 8), float("nan"), dtype=torch.float16, device="cuda")      # pitch 1008: TMA
+    capi_gemm(Ad, Bd, cid, C=big[:M, :N], ldc=N + 8, M=M, N=N, K=K)
+    odd = torch.full((M + 3, N + 1), float("nan"), dtype=torch.float16, device="cuda")      # pitch 1001: plain
+    capi_gemm(Ad, Bd, cid, C=odd[:M, :N], ldc=N + 1, M=M, N=N, K=K)
+    assert_close(big[:M, :N], ref, K, f"TMA-stored C tm {tm} tn {tn} S {split}")
+    assert torch.equal(big[:M, :N].view(torch.int16), odd[:M, :N].view(torch.int16)), "C paths differ"
+    assert torch.isnan(big[:M, N:].float()).all() and torch.isnan(big[M:].float()).all(), "TMA wrote outside C"
+    assert torch.isnan(odd[:M, N:].float()).all() and torch.isnan(odd[M:].float()).all(), "wrote outside C"
