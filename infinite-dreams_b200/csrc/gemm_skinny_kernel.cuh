@@ -14,12 +14,16 @@
 //  * split-K inside a thread-block cluster: the S CTAs of a cluster own the
 //    same TN columns and S consecutive K ranges.  CTA r owns columns
 //    [r*TN/S, (r+1)*TN/S) of the block.  After a cluster barrier (every
-//    pipeline drained), each CTA stores its fp32 accumulator values straight
-//    from TMEM into the owner's idle pipeline buffers through distributed
-//    shared memory (posted stores, one slot per sender); after a second
-//    barrier each owner sums its S slots in rank order (deterministic) from
-//    its own shared memory and stores C.  No workspace, no atomics, no
-//    second pass over global memory, no remote loads.
+//    accumulator complete), each CTA stores its fp32 accumulator values
+//    straight from TMEM into the owner's idle pipeline buffers through
+//    distributed shared memory (posted stores, one slot per sender); after a
+//    second barrier each owner sums its S slots in rank order
+//    (deterministic) from its own shared memory and stores C.  No workspace,
+//    no atomics, no second pass over global memory, no remote loads;
+//  * the finished block is staged as fp16 and written by TMA stores when C
+//    is TMA-addressable.  A cluster of one stages straight from TMEM, with no
+//    cluster barrier, through code that its epilogue warps run once "dry"
+//    during the mainloop (skinny_stage_c).
 //
 // Roles as in gemm_sm100_kernel.cuh: warp 0 TMA producer, warp 1 TMEM owner
 // and MMA issuer, warps 2..5 read the accumulator.  Every mbarrier wait is
@@ -69,6 +73,62 @@ struct SkinnyPlan {
 // stored as ns / box boxes of [TM rows x box columns], staged one after the
 // other, each row-major.  The tensor map's box is [min(ns, 256) x TM].
 __host__ __device__ constexpr int skinny_c_box(int ns) { return ns < 256 ? ns : 256; }
+
+// Copies a cluster-of-one accumulator to the fp16 staging tile of its TMA
+// store ([TM][TN] in boxes of skinny_c_box(TN) columns, each row-major),
+// applying the fused epilogue when `epi`.  One thread's TMEM lane holds
+// column n_local of every 128-column MMA block.
+//
+// Not inlined, so that both calls run the same instructions.  The epilogue
+// warps first call it "dry" while the mainloop runs: keep = 0 sends every
+// store to a 2-byte sink and no TMEM is read.  That brings this code into
+// the instruction cache.  Fetched cold at the very end of a launch, while
+// the memory system is still saturated, the unrolled copy of 64 rows took
+// ~3 us.  The second call (keep = ~0) stages the real values.  Both calls
+// take run-time arguments, so the compiler has no constant to specialise a
+// copy of the function on.
+template <int TM, int TN>
+__device__ __noinline__ void skinny_stage_c(uint32_t taddr, int n_local, uint32_t dst, uint32_t keep, int m0,
+                                            int n0, int M, int N, int epi, int act, float alpha, float beta,
+                                            const __half* D, long long ldd, const __half* bias) {
+  constexpr int kNB = TN / kSkinnyN;
+  constexpr int kBox = skinny_c_box(TN);
+#pragma unroll
+  for (int c32 = 0; c32 < (kNB * TM + 31) / 32; ++c32) {
+    uint32_t v[32];
+    if (keep) {
+      tmem_ld_32x32b_x32(taddr + c32 * 32, v);
+      tmem_ld_wait();
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = 0u;
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int col = c32 * 32 + i;
+      if (col < kNB * TM) {
+        // accumulator h holds TMEM columns [h*TM, (h+1)*TM): row m of C for
+        // column h*128 + n_local of the block
+        const int h = col / TM, m = col - h * TM;
+        const int bcol = h * kSkinnyN + n_local;
+        float x = __uint_as_float(v[i]);
+        if (epi) {
+          const int gm = m0 + m, gn = n0 + bcol;
+          float d = 0.0f, b = 0.0f;
+          if (gm < M && gn < N) {
+            if (beta != 0.0f) d = __half2float(D[static_cast<long long>(gm) * ldd + gn]);
+            if (bias != nullptr) b = __half2float(bias[gn]);
+          }
+          float y = alpha * x;
+          if (beta != 0.0f) y = fmaf(beta, d, y);
+          x = apply_act(y + b, act);
+        }
+        const uint32_t off = static_cast<uint32_t>(((bcol / kBox) * (TM * kBox) + m * kBox + bcol % kBox) * 2);
+        st_shared_u16(dst + (off & keep), __half_as_ushort(__float2half_rn(x)));
+      }
+    }
+  }
+}
 
 template <int TM, int TN, int STAGES>
 __global__ void __launch_bounds__(kNumThreads, 1)
@@ -121,6 +181,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
   griddep_wait();  // global memory only after the previous grid in the stream has completed
   bool acc_ok = true;  // epilogue warps: the accumulator barrier completed in time
+  // producer: ring position after its last load, for the drain at the end
+  int drain_stage = 0, drain_issued = 0;
+  uint32_t drain_phase = 0;
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -162,19 +225,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         *abort_flag = 1;
         atomicOr(p.err, kDevErrTimeoutProducer);
       }
-      // the last min(issued, STAGES) fills must land before their buffers are reused
-      const int outstanding = issued < STAGES ? issued : STAGES;
-      for (int i = 0; i < outstanding; ++i) {
-        stage = (stage == 0) ? STAGES - 1 : stage - 1;
-        if (stage == STAGES - 1) phase ^= 1u;
-        const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(&full_bar[stage], phase)) {
-          if (globaltimer_ns() - t0 > kWaitLimitNs) {
-            atomicOr(p.err, kDevErrTimeoutTeardown);
-            break;
-          }
-        }
-      }
+      // The last fills are drained only after an abort, at the very end of
+      // the kernel.  In a normal run the MMA thread waited for every fill
+      // issued here before its MMAs retired and the accumulator completed, so
+      // none is in flight once the buffers are reused.  After an abort the
+      // drain keeps the CTA, and its shared memory, alive until every fill
+      // has landed.  Draining here, every time, put this thread last at the
+      // first barrier after the mainloop: it saw the final fill ~0.8 us after
+      // the MMA thread had consumed it.
+      drain_stage = stage;
+      drain_phase = phase;
+      drain_issued = issued;
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -224,6 +285,15 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       }
     }
   } else {
+    if (S == 1 && p.c_tma) {
+      // dry staging pass while the mainloop runs (see skinny_stage_c);
+      // p.M < 0 never holds, it only keeps the arguments run-time values
+      const uint32_t sink = smem_u32(smem + Plan::kOffMisc + 8);
+      const bool never = p.M < 0;
+      skinny_stage_c<TM, TN>(tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16), (warp & 3) * 32 + lane,
+                             sink, never ? ~0u : 0u, m0, n0, p.M, p.N, never ? p.epi : 0, p.act, p.alpha, p.beta,
+                             p.D, p.ldd, p.bias);
+    }
     // ------------------------------------------------------------ wait for the accumulator
     // One lane per warp polls the barrier through the whole mainloop; the
     // others wait at the shuffle instead of competing for issue slots with
@@ -250,35 +320,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     constexpr int kBox = skinny_c_box(TN);
     __half* stage = reinterpret_cast<__half*>(smem);
     if (warp >= 2 && acc_ok) {
-      const int ew = warp & 3;
-      const int n_local = ew * 32 + lane;
-#pragma unroll
-      for (int c32 = 0; c32 < (Plan::kNB * TM + 31) / 32; ++c32) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(ew * 32) << 16) + c32 * 32, v);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int col = c32 * 32 + i;
-          if (col < Plan::kNB * TM) {
-            // accumulator h holds TMEM columns [h*TM, (h+1)*TM): row m of C
-            // for column h*128 + n_local of the block
-            const int h = col / TM, m = col - h * TM;
-            const int bcol = h * kSkinnyN + n_local;
-            float x = __uint_as_float(v[i]);
-            if (p.epi) {
-              const int gm = m0 + m, gn = n0 + bcol;
-              float d = 0.0f, b = 0.0f;
-              if (gm < p.M && gn < p.N) {
-                if (p.beta != 0.0f) d = __half2float(p.D[static_cast<long long>(gm) * p.ldd + gn]);
-                if (p.bias != nullptr) b = __half2float(p.bias[gn]);
-              }
-              x = epilogue_value(p, x, d, b);
-            }
-            stage[(bcol / kBox) * (TM * kBox) + m * kBox + bcol % kBox] = __float2half_rn(x);
-          }
-        }
-      }
+      skinny_stage_c<TM, TN>(tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16), (warp & 3) * 32 + lane,
+                             smem_u32(stage), ~0u, m0, n0, p.M, p.N, p.epi, p.act, p.alpha, p.beta, p.D, p.ldd,
+                             p.bias);
       fence_proxy_async_smem();
     }
     tc_fence_before();
@@ -296,8 +340,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ cluster reduction
-    // Barrier 1: every CTA of the cluster has drained its pipeline (all fills
-    // landed, all MMAs retired), so its buffers may now receive partial tiles.
+    // Barrier 1: every CTA of the cluster has completed its accumulator (all
+    // MMAs retired, so every fill they consumed has landed), so its buffers
+    // may now receive partial tiles.
     tc_fence_before();
     __syncwarp();
     cluster_sync();
@@ -398,6 +443,23 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc<1>(tmem_base, Plan::kTmemCols);
+  }
+  if (warp == 0 && lane == 0 && *abort_flag) {
+    // after an abort: the last min(issued, STAGES) fills land before this CTA
+    // exits (every role raises the flag before the barriers above, so the
+    // producer reads its final value here)
+    const int outstanding = drain_issued < STAGES ? drain_issued : STAGES;
+    for (int i = 0; i < outstanding; ++i) {
+      drain_stage = (drain_stage == 0) ? STAGES - 1 : drain_stage - 1;
+      if (drain_stage == STAGES - 1) drain_phase ^= 1u;
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(&full_bar[drain_stage], drain_phase)) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          atomicOr(p.err, kDevErrTimeoutTeardown);
+          break;
+        }
+      }
+    }
   }
 }
 

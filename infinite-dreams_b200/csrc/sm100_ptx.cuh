@@ -139,6 +139,11 @@ __device__ __forceinline__ uint32_t cluster_id_x() {
   return r;
 }
 
+// 2-byte store to this CTA's shared memory at a 32-bit shared address.
+__device__ __forceinline__ void st_shared_u16(uint32_t saddr, unsigned short v) {
+  asm volatile("st.shared.u16 [%0], %1;" ::"r"(saddr), "h"(v) : "memory");
+}
+
 // 4-byte store into shared memory of a CTA in the cluster (posted: the
 // thread does not wait for it; a cluster barrier with release/acquire
 // semantics makes it visible to the owner).
