@@ -7,9 +7,9 @@
 //
 //  * operands swapped: the MMA computes C^T = B^T A^T, so 128 columns of C
 //    fill the 128 TMEM lanes (MMA M = 128) and the few rows of A are the MMA
-//    N (TM = 16, 32 or 64).  A cluster owns TN = 128 or 256 columns of C
-//    (one or two MMAs per K step).  Per pipeline stage a CTA loads a
-//    [64 K x TN] tile of B (16 or 32 KiB, all useful) and a [TM x 64 K]
+//    N (TM = 16, 32 or 64).  A cluster owns TN = 128, 256 or 512 columns of
+//    C (one, two or four MMAs per K step).  Per pipeline stage a CTA loads a
+//    [64 K x TN] tile of B (16, 32 or 64 KiB, all useful) and a [TM x 64 K]
 //    tile of A (2-8 KiB), so the ring holds ~200 KiB of B in flight;
 //  * split-K inside a thread-block cluster: the S CTAs of a cluster own the
 //    same TN columns and S consecutive K ranges.  CTA r owns columns
@@ -27,7 +27,8 @@
 //
 // Roles as in gemm_sm100_kernel.cuh: warp 0 TMA producer, warp 1 TMEM owner
 // and MMA issuer, warps 2..5 read the accumulator.  Every mbarrier wait is
-// bounded; both cluster barriers are reached by every thread on every path.
+// bounded; on the cluster path both cluster barriers are reached by every
+// thread on every path, the abort path included.
 #pragma once
 #include <atomic>
 #include <cuda_runtime.h>
