@@ -188,8 +188,7 @@ int gemm_selftest_wait_timeout(uint64_t limit_ns, uint64_t* waited_ns);
  * stream capture); each call clears the ticket region on `stream`.  All
  * calls on a device share the array, so calls whose kernels overlap on the
  * GPU race; serialise them.  Nothing here calls cudaMalloc or cudaFree.
- * No counterpart in the reference (its extension allocated C through
- * torch and used no scratch, src/gemm_ext.cpp:35). */
+ * No counterpart in the reference. */
 int gemm_launch_noalloc(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
                         int64_t ldb, int64_t ldc, int cfg_id, void* stream);
 

@@ -64,9 +64,14 @@ extern "C" int gemm_launch_noalloc(const void* A, const void* B, void* C, int64_
   }
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+  if (e != cudaSuccess) {
     idb::record_last_error(std::string("gemm_launch_noalloc: cudaGetDevice: ") + cudaGetErrorString(e));
     return GEMM_ERR_CUDA;
+  }
+  if (dev < 0 || dev >= kMaxDevices) {
+    idb::record_last_error("gemm_launch_noalloc: device index " + std::to_string(dev) + " out of range [0, " +
+                           std::to_string(kMaxDevices) + ")");
+    return GEMM_ERR_UNSUPPORTED;
   }
   // Set-up, once per device, with that device current.
   std::call_once(g_scratch_once[dev], [dev] {

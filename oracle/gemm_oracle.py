@@ -31,10 +31,14 @@ _lib: Optional[ctypes.CDLL] = None
 
 
 def build(reference_src: Optional[str] = None) -> None:
-    """Builds the C oracle, and the reference bank when its source is present."""
+    """Builds the C oracle, and the reference bank when its source is given.
+
+    ``reference_src`` (or the ``REFERENCE_SRC`` environment variable) names
+    the reference's ``src/`` directory; without one, or when it holds no
+    ``gemm_kernels.cuh``, only the C oracle is built."""
     subprocess.run(["make", "-s", "-C", str(ORACLE_DIR)], check=True)
-    src = reference_src or "/root/reference/src"
-    if Path(src, "gemm_kernels.cuh").exists():
+    src = reference_src or os.environ.get("REFERENCE_SRC")
+    if src and Path(src, "gemm_kernels.cuh").exists():
         subprocess.run(["make", "-s", "-C", str(ORACLE_DIR), "ref", f"REFERENCE_SRC={src}"], check=True)
 
 

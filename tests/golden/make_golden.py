@@ -1,6 +1,6 @@
 """Generates tests/golden/ref_gemm_golden.npz from the reference kernel itself.
 
-Run on a B200 after `make -C oracle ref` (which compiles the reference's
+Run on a B200 after `make -C oracle ref REFERENCE_SRC=<reference src/>` (which compiles the reference's
 src/gemm_kernels.cuh for sm_100a into oracle/_ref/libref_gemm.so):
 
     python tests/golden/make_golden.py
@@ -60,7 +60,7 @@ def main() -> None:
 
     lib = oracle.load_ref()
     if lib is None:
-        raise SystemExit("oracle/_ref/libref_gemm.so is missing: run `make -C oracle ref` first")
+        raise SystemExit("oracle/_ref/libref_gemm.so is missing: run `make -C oracle ref REFERENCE_SRC=<reference src/>` first")
     cfgs = oracle.ref_cfgs(lib)
     arrays = {}
     names = []

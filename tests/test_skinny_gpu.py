@@ -151,3 +151,32 @@ def test_skinny_tma_store_matches_plain_stores(cuda_device, tm, tn, stages, spli
     assert torch.equal(big[:M, :N].view(torch.int16), odd[:M, :N].view(torch.int16)), "C paths differ"
     assert torch.isnan(big[:M, N:].float()).all() and torch.isnan(big[M:].float()).all(), "TMA wrote outside C"
     assert torch.isnan(odd[:M, N:].float()).all() and torch.isnan(odd[M:].float()).all(), "wrote outside C"
+
+
+@pytest.mark.parametrize("split,tn,stages", [(1, 128, 8), (2, 256, 5), (4, 128, 8)])
+def test_skinny_epilogue_tma_store_matches_plain_stores(cuda_device, split, tn, stages):
+    """The fused epilogue on a TMA-addressable C (pitch a multiple of 8: the staged block goes out by TMA
+    stores) against the same epilogue on an odd pitch (per-thread stores): bit for bit, for clusters of
+    1, 2 and 4, including an in-place update (D is C).  Both match the oracle."""
+    M, N, K = 40, 1536, 2048
+    g = torch.Generator().manual_seed(100 + split)
+    x = (torch.rand((M, K), generator=g) * 2 - 1).half()
+    W = (torch.rand((N, K), generator=g) * 0.1 - 0.05).half()
+    b = (torch.rand((N,), generator=g) - 0.5).half()
+    D = (torch.rand((M, N), generator=g) * 2 - 1).half()
+    cid = _cfg(64, stages, split, tn)
+    xd, Wd = x.cuda(), W.cuda()
+    for act, name in ((0, "none"), (2, "gelu")):
+        ref = oracle.gemm_ex(x.numpy(), W.numpy(), trans_b=True, alpha=0.75, beta=-0.5, D=D.numpy(), bias=b.numpy(),
+                             activation=name)
+        tma_c = torch.full((M, N), float("nan"), dtype=torch.float16, device="cuda")           # pitch 1536: TMA
+        _ex(xd, Wd, M, N, K, 1, cid, alpha=0.75, beta=-0.5, D=D.cuda(), bias=b.cuda(), act=act, C=tma_c)
+        odd = torch.full((M, N + 1), float("nan"), dtype=torch.float16, device="cuda")         # pitch 1537: plain
+        _ex(xd, Wd, M, N, K, 1, cid, alpha=0.75, beta=-0.5, D=D.cuda(), bias=b.cuda(), act=act, C=odd[:, :N])
+        assert_close(tma_c, ref, K, f"TMA-stored epilogue {name} S {split}")
+        assert torch.equal(tma_c.view(torch.int16), odd[:, :N].view(torch.int16)), f"C paths differ ({name})"
+        assert torch.isnan(odd[:, N:].float()).all(), "wrote outside the C view"
+        # in place: C starts as D and is overwritten with act(alpha * acc + beta * C + b)
+        inplace = D.cuda().clone()
+        _ex(xd, Wd, M, N, K, 1, cid, alpha=0.75, beta=-0.5, D=inplace, bias=b.cuda(), act=act, C=inplace)
+        assert torch.equal(inplace.view(torch.int16), tma_c.view(torch.int16)), f"in-place update differs ({name})"

@@ -60,6 +60,10 @@ def test_noalloc_matches_gemm_launch_two_calls_in_a_row(cuda_device):
         second = _noalloc(Ad, Bd, cid, M, N, K)               # the array keeps the first call's contents
         assert_close(first, ref, K, f"noalloc first call {M}x{N}x{K}")
         assert_close(second, ref, K, f"noalloc second call {M}x{N}x{K}")
+        # Same kernels, same K order: a stale partial or ticket left in the
+        # shared array by the first call would show up as a bit difference.
+        assert torch.equal(first.view(torch.int16), expect.view(torch.int16)), f"first call {M}x{N}x{K}"
+        assert torch.equal(second.view(torch.int16), expect.view(torch.int16)), f"second call {M}x{N}x{K}"
     from infinite_dreams import infinite_dreams_ext as ext
     ext.check_device_errors()
 
