@@ -5,17 +5,31 @@ fp32 accumulate, fp16 out, A and B uniform[-1,1] from a seed.  A is split into
 N contiguous row blocks, one per rank (one process per GPU); B is generated on
 rank 0 and broadcast once at set-up (untimed); each rank computes its C rows
 with no data-path collective.  Total work is fixed, so scaling is "strong".
-A "step" is one GEMM over the local row block.  The optional NCCL all-gather
-of C (``--allgather``) is timed separately and reported under "allgather": as a
-GEMM followed by one NCCL all-gather, as a two-chunk pipeline of both, and
-fused into the GEMM (tiles stored into every rank's C over NVLink).
+A "step" is one GEMM over the local row block.
+
+At N > 1 the output exchange (all-gather of the C row blocks, so that every
+rank ends with the whole C) is timed after the GEMM loop and reported under
+"allgather": a GEMM followed by one NCCL all-gather, a two-chunk pipeline of
+both, and the exchange fused into the GEMM (every tile stored into every
+rank's C over NVLink from the epilogue).  Every result -- the local C block
+and each gathered C -- is checked outside the timed regions on sampled rows
+against the oracle (the CPU restatement of the reference kernel) under
+|err| <= 1e-2*sqrt(K/1024)*max|C_ref| + 1e-3; "parity" in the line is true
+only if every check on every rank passed.
+
+At N = 1 the line also carries "shapes": every other workload shape (the
+reference tuner's 5 shapes with their mean, 512^3, the square sweep, the
+skinny and the irregular shapes) through the dispatch table, each
+parity-checked the same way and timed one launch after an L2 flush, back to
+back, and replayed from a CUDA graph, with cuBLAS (torch.matmul) timed beside.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
   torchrun --nproc-per-node N bench.py --gpus N ...
 
 ``--impl reference`` times the CPU restatement of the reference kernel (the
 oracle) on the host cores over a bounded sample of rows of the same workload;
-under torchrun only rank 0 runs it.
+under torchrun only rank 0 runs it.  It also times the reference's own CUDA
+kernel (compiled from its source) on every workload shape, for information.
 """
 from __future__ import annotations
 
@@ -28,7 +42,7 @@ import sys
 import threading
 import time
 from pathlib import Path
-from typing import Dict, List, Optional
+from typing import Dict, List, Optional, Tuple
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "infinite-dreams_b200"))
@@ -39,6 +53,11 @@ NOMINAL_FP16_TFLOPS = 2250.0
 NOMINAL_HBM_GBS = 8000.0
 FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0}
 SIZE = 16384
+# A timed region at least this long runs under the power cap, and is set
+# against the sustained GEMM peak; a shorter one against the burst peak.
+SUSTAINED_REGION_MS = 2000.0
+PARITY_ROWS = 32          # sampled rows of each checked C (all ranks' blocks together)
+SHAPE_SETS = ["default", "single", "square", "skinny", "irregular"]
 
 
 def parse() -> argparse.Namespace:
@@ -51,13 +70,16 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--cfg", type=int, default=None, help="menu cfg_id (default: dispatch table / heuristic)")
     ap.add_argument("--knobs", type=str, default=None,
                     help="kernel config as its knob tuple, e.g. 256,512,64,4,2,1,8,1 (stable across menu changes)")
-    ap.add_argument("--allgather", action="store_true", help="also time the NCCL all-gather of C")
+    ap.add_argument("--no-allgather", action="store_true", help="N > 1: skip the timed output exchange")
+    ap.add_argument("--allgather", action="store_true", help=argparse.SUPPRESS)   # the default at N > 1
+    ap.add_argument("--no-shapes", action="store_true", help="N = 1: skip the per-shape block")
+    ap.add_argument("--shape-sets", default=",".join(SHAPE_SETS))
+    ap.add_argument("--no-parity", action="store_true", help="skip the oracle checks of the outputs")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU-baseline sample budget")
-    ap.add_argument("--ref-shapes", action="store_true",
-                    help="reference arm: also time the reference's CUDA kernel (built from its source) on the GPU "
-                         "for every workload shape")
+    ap.add_argument("--no-ref-shapes", action="store_true",
+                    help="reference arm: skip timing the reference's CUDA kernel on the workload shapes")
     return ap.parse_args()
 
 
@@ -70,69 +92,236 @@ def peaks() -> Dict[str, object]:
     return dict(FALLBACK_PEAKS, source="fallback")
 
 
+def host_threads() -> int:
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except AttributeError:  # pragma: no cover
+        return os.cpu_count() or 1
+
+
 # ----------------------------------------------------------------------------- clocks
+_REASONS = {  # NVML clock event reason bits that the timing rules name
+    0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+    0x80: "hw_power_brake_slowdown",
+}
+
+
 class ClockSampler:
-    """Samples nvidia-smi clocks / throttle reasons in the background."""
+    """Samples the SM clock, power and clock event reasons of one GPU in a
+    background thread, every few milliseconds, each sample with its host
+    timestamp, so that a window (the timed region) can be cut out of the
+    record afterwards.  Reads NVML; falls back to an ``nvidia-smi`` loop."""
 
-    FIELDS = ["index", "clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.active",
-              "clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
-              "clocks_event_reasons.sw_thermal_slowdown", "clocks_event_reasons.sw_power_cap"]
+    SMI_FIELDS = ["clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.hw_slowdown",
+                  "clocks_event_reasons.hw_thermal_slowdown", "clocks_event_reasons.sw_thermal_slowdown",
+                  "clocks_event_reasons.sw_power_cap"]
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.rows: List[List[str]] = []
-        self.proc: Optional[subprocess.Popen] = None
-        self.thread: Optional[threading.Thread] = None
+    def __init__(self, cuda_index: int, period_s: float = 0.002):
+        self.cuda_index = cuda_index
+        self.period = period_s
+        self.samples: List[Tuple[float, float, float, List[str]]] = []   # (t, sm MHz, W, reasons)
+        self.max_mhz: Optional[float] = None
+        self.source = "none"
+        self._stop = threading.Event()
+        self._thread: Optional[threading.Thread] = None
+        self._proc: Optional[subprocess.Popen] = None
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        try:
+            pr = torch.cuda.get_device_properties(self.cuda_index)
+            bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+            return pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml.nvmlDeviceGetHandleByIndex(self.cuda_index)
 
     def start(self) -> None:
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", "--query-gpu=" + ",".join(self.FIELDS),
+            import pynvml
+
+            h = self._nvml_handle()
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            self.source = "nvml"
+            self._thread = threading.Thread(target=self._poll_nvml, args=(h,), daemon=True)
+            self._thread.start()
+            return
+        except Exception:
+            pass
+        try:
+            self._proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.cuda_index}", "--query-gpu=" + ",".join(self.SMI_FIELDS),
                  "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
-            self.proc = None
             return
-        self.thread = threading.Thread(target=self._read, daemon=True)
-        self.thread.start()
+        self.source = "nvidia-smi"
+        self._thread = threading.Thread(target=self._read_smi, daemon=True)
+        self._thread.start()
 
-    def _read(self) -> None:
-        assert self.proc is not None and self.proc.stdout is not None
-        for line in self.proc.stdout:
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) == len(self.FIELDS):
-                self.rows.append(parts)
+    def _poll_nvml(self, h) -> None:
+        import pynvml
 
-    def stop(self) -> Dict[str, object]:
-        if self.proc is not None:
-            self.proc.terminate()
+        while not self._stop.is_set():
             try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-        if self.thread is not None:
-            self.thread.join(timeout=5)
-        if not self.rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+                t = time.monotonic()
+                mhz = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                watts = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+                bits = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(h))
+                self.samples.append((t, mhz, watts, [n for b, n in _REASONS.items() if bits & b]))
+            except Exception:
+                return
+            self._stop.wait(self.period)
 
-        def num(x: str) -> Optional[float]:
-            try:
-                return float(x)
-            except ValueError:
-                return None
-
-        power = [num(r[3]) or 0.0 for r in self.rows]
-        pmax = max(power)
-        loaded = [r for r, pw in zip(self.rows, power) if pw >= 0.5 * pmax] or self.rows
-        sm = [num(r[1]) for r in loaded if num(r[1]) is not None]
-        reasons = set()
+    def _read_smi(self) -> None:
+        assert self._proc is not None and self._proc.stdout is not None
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in loaded:
-            for name, v in zip(names, r[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": num(loaded[0][2]),
-                "reasons": sorted(reasons), "samples": len(loaded), "power_w_max": pmax}
+        for line in self._proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) != len(self.SMI_FIELDS):
+                continue
+            try:
+                mhz, mx, watts = float(parts[0]), float(parts[1]), float(parts[2])
+            except ValueError:
+                continue
+            self.max_mhz = mx
+            self.samples.append((time.monotonic(), mhz, watts,
+                                 [n for n, v in zip(names, parts[3:]) if v.lower().startswith("active")]))
+
+    def stop(self) -> None:
+        self._stop.set()
+        if self._proc is not None:
+            self._proc.terminate()
+            try:
+                self._proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._proc.kill()
+        if self._thread is not None:
+            self._thread.join(timeout=5)
+
+    def window(self, t0: float, t1: float, kernel_ms: Optional[float] = None) -> Dict[str, object]:
+        """Summary of the samples taken between host times t0 and t1."""
+        inside = [s for s in self.samples if t0 <= s[0] <= t1]
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"], "samples": 0,
+                    "window_ms": (t1 - t0) * 1e3, "sampler": self.source}
+        mhz = statistics.median(s[1] for s in inside)
+        reasons = sorted({r for s in inside for r in s[3]})
+        out = {"sm_mhz": mhz, "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(inside),
+               "window_ms": (t1 - t0) * 1e3, "sm_mhz_min": min(s[1] for s in inside),
+               "power_w_median": statistics.median(s[2] for s in inside),
+               "power_w_max": max(s[2] for s in inside), "sampler": self.source,
+               "reason_samples": {r: sum(1 for s in inside if r in s[3]) for r in reasons}}
+        if kernel_ms is not None:
+            # clock-normalised kernel time: ms x median MHz (lower is better per clock)
+            out["kernel_ms_x_mhz"] = kernel_ms * mhz
+        return out
+
+
+# ----------------------------------------------------------------------------- oracle checks
+def _block_rows(M_total: int, world: int, per_block: int) -> List[List[int]]:
+    """Sampled rows of each rank's block: its first and last row and evenly
+    spread rows between them (global row indices)."""
+    rows = M_total // world
+    out = []
+    for r in range(world):
+        lo, hi = r * rows, (r + 1) * rows - 1
+        n = max(2, min(per_block, rows))
+        picks = sorted({lo + (hi - lo) * i // (n - 1) for i in range(n)})
+        out.append(picks)
+    return out
+
+
+class RowChecker:
+    """Reference values of sampled rows of the sharded 16384^3 GEMM, from the
+    oracle, for checking the local C block and every gathered C."""
+
+    def __init__(self, make_block, B, world: int, rank: int, K: int, threads: int):
+        import numpy as np
+        import torch
+
+        import oracle
+
+        self.world, self.rank, self.K = world, rank, K
+        per_block = max(2, PARITY_ROWS // world)
+        rows = None
+        a_rows = []
+        self.blocks: List[List[int]] = []
+        for r in range(world):
+            A_r = make_block(r)
+            n = A_r.shape[0]
+            if rows is None:
+                rows = n
+                self.blocks = _block_rows(n * world, world, per_block)
+            idx = [g - r * rows for g in self.blocks[r]]
+            a_rows.append(A_r[idx].cpu().numpy())
+            del A_r
+            torch.cuda.empty_cache()
+        self.rows_per_block = rows
+        self.n_rows = sum(len(b) for b in self.blocks)
+        A_s = np.concatenate(a_rows, 0)
+        self.ref = oracle.gemm_f16(A_s, B.cpu().numpy(), threads=threads).astype(np.float32)
+        self.tol = oracle.tolerance(self.ref, K)
+
+    def _compare(self, got, ref) -> Tuple[bool, float]:
+        import numpy as np
+
+        got = got.float().cpu().numpy()
+        if not np.isfinite(got).all():
+            return False, float("inf")
+        err = float(np.max(np.abs(got - ref))) if got.size else 0.0
+        return err <= self.tol, err
+
+    def check_local(self, C_local) -> Tuple[bool, float]:
+        idx = [g - self.rank * self.rows_per_block for g in self.blocks[self.rank]]
+        n0 = sum(len(b) for b in self.blocks[:self.rank])
+        ref = self.ref[n0:n0 + len(idx)]
+        return self._compare(C_local[idx], ref)
+
+    def check_full(self, C_full) -> Tuple[bool, float]:
+        idx = [g for b in self.blocks for g in b]
+        return self._compare(C_full[idx], self.ref)
+
+
+def _parity_summary(results: Dict[str, Tuple[bool, float]], checker: "RowChecker", world: int,
+                    dev) -> Dict[str, object]:
+    """Combines this rank's checks with every other rank's (all must pass)."""
+    import torch
+    import torch.distributed as dist
+
+    names = sorted(results)
+    ok = torch.tensor([1.0 if results[n][0] else 0.0 for n in names], device=dev, dtype=torch.float64)
+    err = torch.tensor([results[n][1] for n in names], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        dist.all_reduce(err, op=dist.ReduceOp.MAX)
+    return {"ok": bool(ok.min().item() > 0.5) if names else None,
+            "checks": {n: {"ok": bool(ok[i].item() > 0.5), "max_abs_err": float(err[i].item())}
+                       for i, n in enumerate(names)},
+            "tolerance": checker.tol, "rows_checked_per_gathered_c": checker.n_rows,
+            "rows_checked_per_local_block": len(checker.blocks[checker.rank]),
+            "rule": "|err| <= 1e-2*sqrt(K/1024)*max|C_ref| + 1e-3 on sampled rows (first, last and spread "
+                    "rows of every rank's block) against the oracle"}
+
+
+def shape_checker(threads: int):
+    """check(M, N, K, A, B, C) for bench_shapes.run: sampled rows (all rows
+    when M <= 64) of C against the oracle."""
+    def check(M, N, K, A, B, C):
+        import numpy as np
+
+        import oracle
+
+        n = M if M <= 64 else 48
+        idx = sorted({(M - 1) * i // max(n - 1, 1) for i in range(n)})
+        ref = oracle.gemm_f16(A[idx].cpu().numpy(), B.cpu().numpy(), threads=threads).astype(np.float32)
+        got = C[idx].float().cpu().numpy()
+        tol = oracle.tolerance(ref, K)
+        err = float(np.max(np.abs(got - ref))) if np.isfinite(got).all() else float("inf")
+        return {"ok": bool(err <= tol), "max_abs_err": err, "tolerance": tol, "rows": len(idx)}
+    return check
 
 
 # ----------------------------------------------------------------------------- CPU oracle timing
@@ -143,9 +332,10 @@ def cpu_oracle_sample(size: int, budget_s: float, seed: int = 0) -> Dict[str, ob
 
     import oracle
 
-    threads = len(os.sched_getaffinity(0))
+    threads = host_threads()
     rng = np.random.default_rng(seed)
     B = rng.uniform(-1.0, 1.0, size=(size, size)).astype(np.float16)
+
     def run(r: int) -> float:
         A = rng.uniform(-1.0, 1.0, size=(r, size)).astype(np.float16)
         t0 = time.perf_counter()
@@ -173,9 +363,10 @@ def run_reference(args: argparse.Namespace) -> None:
     import oracle
 
     size = args.size
-    threads = len(os.sched_getaffinity(0))
+    threads = host_threads()
     rng = np.random.default_rng(0)
     B = rng.uniform(-1.0, 1.0, size=(size, size)).astype(np.float16)
+
     # Size one step so that the whole --steps/--warmup run takes ~90 s of host
     # work: time(r) = fixed + r * per_row, fitted from two probes.
     def run(r: int) -> float:
@@ -211,7 +402,7 @@ def run_reference(args: argparse.Namespace) -> None:
         "note": ("the reference's path is a CUDA kernel with no CPU implementation; this arm times the "
                  "oracle, a C restatement of that kernel's arithmetic (bit-exact to it), on the host cores"),
     }
-    bank = reference_cuda_bank(size, args.ref_shapes)
+    bank = reference_cuda_bank(size, not args.no_ref_shapes)
     if bank is not None:
         line["reference_cuda_bank"] = bank
     emit(line)
@@ -221,8 +412,10 @@ def reference_cuda_bank(size: int, all_shapes: bool) -> Optional[Dict[str, objec
     """Times the reference's own SIMT kernel (src/gemm_kernels.cuh, compiled
     from its source into oracle/_ref) on the GPU: the bench workload and, with
     all_shapes, every workload shape, each with the best of the instantiated
-    tile configurations, back to back like the reference's tuner.
-    Informational; the arm's value is the CPU oracle."""
+    tile configurations, back to back like the reference's tuner; and the
+    reference's published metric, the mean ms over its tuner's 5 shapes
+    (infinite_dreams/sizes.py:4-11).  Informational; the arm's value is the
+    CPU oracle."""
     try:
         import torch
     except ImportError:  # pragma: no cover
@@ -265,14 +458,20 @@ def reference_cuda_bank(size: int, all_shapes: bool) -> Optional[Dict[str, objec
         return out
 
     res = {"kernel": "gemm_tiled_reg (reference SIMT bank, -O3 --use_fast_math, sm_100a)",
+           "timing": "best instantiated tile per shape, back to back on warm caches (the reference tuner's way)",
            "workload": dict(best(size, size, size, 1) or {}, shape=[size, size, size])}
     if all_shapes:
         res["shapes"] = {}
         for name, shapes in shape_sets().items():
-            if name == "large":
+            if name in ("large", "sharded"):
                 continue
             for (M, N, K) in shapes:
-                res["shapes"][f"{M}x{N}x{K}"] = best(M, N, K, 3)
+                key = f"{M}x{N}x{K}"
+                if key not in res["shapes"]:
+                    res["shapes"][key] = best(M, N, K, 3)
+        dflt = [res["shapes"].get(f"{M}x{N}x{K}") for (M, N, K) in shape_sets()["default"]]
+        if all(d is not None for d in dflt):
+            res["default_sizes_mean_ms"] = sum(d["ms"] for d in dflt) / len(dflt)
     return res
 
 
@@ -280,7 +479,7 @@ def workload_config(size: int, n: int, knobs: Optional[Dict[str, int]]) -> Dict[
     cfg = {"workload": f"gemm {size}x{size}x{size} fp16 (fp32 accumulate), A row-sharded over {n} rank(s), "
                        f"B replicated",
            "M": size, "N": size, "K": size, "rows_per_rank": size // n, "inputs": "uniform[-1,1], seeded",
-           "parallelism": f"M-row shards x{n}, no data-path collective",
+           "parallelism": f"M-row shards x{n}, no data-path collective in the timed GEMM loop",
            "l2": "inputs larger than L2 (A block >= 64 MiB, B 512 MiB): no flush needed"}
     if knobs is not None:
         cfg["kernel_cfg"] = knobs
@@ -318,11 +517,15 @@ def run_ours(args: argparse.Namespace) -> None:
         cfg_id = args.cfg if args.cfg is not None else dispatch.lookup(M, N, K)
     knobs = dict(zip(ext.CFG_COLUMNS, ext.gemm_cfg_table_cpu()[cfg_id].tolist()))
 
-    # inputs: rank r's A block comes from the seed (0, r); B from rank 0, broadcast
-    g = torch.Generator(device=dev)
-    g.manual_seed(1000 + rank)
-    A = torch.rand((M, K), generator=g, device=dev, dtype=torch.float32).mul_(2).sub_(1).to(torch.float16)
+    # inputs: rank r's A block comes from the seed 1000 + r; B from rank 0, broadcast
+    def make_block(r: int) -> torch.Tensor:
+        g = torch.Generator(device=dev)
+        g.manual_seed(1000 + r)
+        return torch.rand((M, K), generator=g, device=dev, dtype=torch.float32).mul_(2).sub_(1).to(torch.float16)
+
+    A = make_block(rank)
     if rank == 0:
+        g = torch.Generator(device=dev)
         g.manual_seed(7)
         B = torch.rand((K, N), generator=g, device=dev, dtype=torch.float32).mul_(2).sub_(1).to(torch.float16)
     else:
@@ -350,6 +553,7 @@ def run_ours(args: argparse.Namespace) -> None:
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
+    host_t0 = time.monotonic()
     t_start.record(stream)
     for s, e in ev:
         s.record(stream)
@@ -357,134 +561,47 @@ def run_ours(args: argparse.Namespace) -> None:
         e.record(stream)
     t_end.record(stream)
     torch.cuda.synchronize()
+    host_t1 = time.monotonic()
     barrier()
-    clocks = sampler.stop()
     ms_local = t_start.elapsed_time(t_end)
     kern_ms_local = sum(s.elapsed_time(e) for s, e in ev) / len(ev)
     tvals = torch.tensor([ms_local, kern_ms_local], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(tvals, op=dist.ReduceOp.MAX)
     ms_total, kern_ms = float(tvals[0]), float(tvals[1])
+    sampler.stop()
+    clocks = sampler.window(host_t0, host_t1, kern_ms_local)
     flops_total = 2.0 * size * size * size * args.steps
     value = flops_total / (ms_total * 1e-3) / 1e12
     ms_per_step = ms_total / args.steps
 
     ext.check_device_errors(local)
 
-    # optional all-gather of C row blocks (NCCL over NVLink), timed on its own
+    # Oracle references for sampled rows (outside every timed region).
+    checks: Dict[str, Tuple[bool, float]] = {}
+    checker = None
+    if not args.no_parity:
+        checker = RowChecker(make_block, B, world, rank, K, max(1, host_threads() // world))
+        checks["gemm_local_block"] = checker.check_local(C)
+
+    # The output exchange: every rank ends with the whole C.
     allgather = None
-    if world > 1 and args.allgather:
-        from infinite_dreams.sharded import sharded_gemm
+    if world > 1 and not args.no_allgather:
+        allgather = time_exchange(args, A, B, C, step, cfg_id, size, rows, N, world, dev, stream, barrier,
+                                  checker, checks)
 
-        Cfull = torch.empty((size, N), device=dev, dtype=torch.float16)
-        n_ag = max(1, min(args.steps, 20))
-
-        def timed(fn) -> float:
-            for _ in range(2):
-                fn()
-            barrier()
-            s0 = torch.cuda.Event(enable_timing=True)
-            s1 = torch.cuda.Event(enable_timing=True)
-            s0.record(stream)
-            for _ in range(n_ag):
-                fn()
-            s1.record(stream)
-            torch.cuda.synchronize()
-            t = torch.tensor([s0.elapsed_time(s1)], device=dev, dtype=torch.float64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            return float(t[0]) / n_ag
-
-        def one_shot():
-            step()
-            dist.all_gather_into_tensor(Cfull, C)
-
-        def pipelined():
-            # two row chunks: the first chunk's all-gather overlaps the second chunk's GEMM
-            sharded_gemm(A, B, M_total=size, gather=True, out=Cfull, chunks=2,
-                         compute=lambda a, b, o: ext.gemm_forward_cfg(
-                             a, b, dispatch.lookup(a.shape[0], b.shape[1], a.shape[1]), out=o))
-
-        def fused():
-            # every tile goes to all ranks' C from the GEMM's epilogue (NVLink stores), then a
-            # one-element all-reduce on the stream marks all ranks' grids complete
-            sharded_gemm(A, B, M_total=size, gather=True, exchange="fused")
-
-        ms_one = timed(one_shot)
-        ms_pipe = timed(pipelined)
-        ms_fused = timed(fused)
-        allgather = {"ms_per_step_gemm_then_allgather": ms_one,
-                     "value_gemm_then_allgather": 2.0 * size ** 3 / (ms_one * 1e-3) / 1e12,
-                     "ms_per_step_pipelined_2_chunks": ms_pipe,
-                     "value_pipelined": 2.0 * size ** 3 / (ms_pipe * 1e-3) / 1e12,
-                     "ms_per_step_fused": ms_fused,
-                     "value_fused": 2.0 * size ** 3 / (ms_fused * 1e-3) / 1e12,
-                     "bytes_received_per_rank": (world - 1) * rows * N * 2, "steps": n_ag}
-        del Cfull
-        from infinite_dreams.sharded import release_peer_buffers
-        release_peer_buffers()
-
-    # End to end through the public op.  Every step copies its own inputs from
-    # pinned host memory and reads its result back; copies run on their own
-    # streams so that step i+1's upload and step i-1's download overlap step
-    # i's GEMM (double-buffered device inputs and outputs).
     e2e = None
     if not args.no_e2e:
-        hA = [A.cpu().pin_memory(), A.cpu().pin_memory()]
-        hB = [B.cpu().pin_memory(), B.cpu().pin_memory()]
-        hC = [torch.empty((M, N), dtype=torch.float16).pin_memory() for _ in range(2)]
-        dA = [torch.empty_like(A) for _ in range(2)]
-        dB = [torch.empty_like(B) for _ in range(2)]
-        dC = [torch.empty_like(C) for _ in range(2)]
-        s_in = torch.cuda.Stream(dev)
-        s_out = torch.cuda.Stream(dev)
-        # 30 steps amortise the pipeline's fill and drain (one upload and one
-        # download that overlap nothing): the steady state is bound by the
-        # 1 GiB upload per step over PCIe (~55 GB/s).
-        e2e_steps = max(2, min(args.steps, 30))
+        e2e = time_e2e(args, A, B, cfg_id, size, rows, N, K, world, rank, dev, stream, barrier)
 
-        def e2e_run(n_steps: int) -> float:
-            loaded = [torch.cuda.Event() for _ in range(2)]
-            computed = [torch.cuda.Event() for _ in range(2)]
-            drained = [torch.cuda.Event() for _ in range(2)]
-            for ev in drained:
-                ev.record(s_out)
-            start_ev = torch.cuda.Event(enable_timing=True)
-            end_ev = torch.cuda.Event(enable_timing=True)
-            start_ev.record(stream)
-            s_in.wait_event(start_ev)
-            s_out.wait_event(start_ev)
-            for i in range(n_steps):
-                b = i % 2
-                with torch.cuda.stream(s_in):
-                    s_in.wait_event(computed[b]) if i >= 2 else None
-                    dA[b].copy_(hA[b], non_blocking=True)
-                    dB[b].copy_(hB[b], non_blocking=True)
-                    loaded[b].record(s_in)
-                stream.wait_event(loaded[b])
-                stream.wait_event(drained[b])
-                ext.gemm_forward_cfg(dA[b], dB[b], cfg_id, out=dC[b])
-                computed[b].record(stream)
-                with torch.cuda.stream(s_out):
-                    s_out.wait_event(computed[b])
-                    hC[b].copy_(dC[b], non_blocking=True)
-                    drained[b].record(s_out)
-            stream.wait_stream(s_out)
-            end_ev.record(stream)
-            torch.cuda.synchronize()
-            return start_ev.elapsed_time(end_ev)
+    pk = peaks()
+    shapes = None
+    if world == 1 and not args.no_shapes:
+        shapes = shapes_block(args, pk)
 
-        e2e_run(2)
-        barrier()
-        t = torch.tensor([e2e_run(e2e_steps)], device=dev, dtype=torch.float64)
-        if world > 1:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_e2e = float(t[0]) / e2e_steps
-        e2e = {"value": 2.0 * size ** 3 / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
-               "h2d_bytes_per_step": (M * K + K * N) * 2 * world, "d2h_bytes_per_step": M * N * 2 * world,
-               "ms_per_step": ms_e2e, "steps": e2e_steps,
-               "path": "pinned host A,B -> device (copy stream), infinite_dreams_ext.gemm_forward_cfg, "
-                       "C -> pinned host (copy stream); uploads/downloads overlap neighbouring steps' GEMMs"}
-        del hA, hB, hC, dA, dB, dC
+    parity = None
+    if checker is not None:
+        parity = _parity_summary(checks, checker, world, dev)
 
     if world > 1:
         dist.barrier(device_ids=[local])
@@ -492,14 +609,18 @@ def run_ours(args: argparse.Namespace) -> None:
     if rank != 0:
         return
 
-    pk = peaks()
-    # The timed region is ~0.5-1 s of back-to-back GEMMs, which runs under the
-    # power cap: the sustained GEMM figure is the matching denominator.
-    peak = float(pk["bf16_tflops_sustained"])
+    # The denominator follows the timed region's length: a region shorter
+    # than SUSTAINED_REGION_MS is mostly above the power cap's settling time,
+    # so it is set against the burst GEMM peak.
+    sustained = ms_total >= SUSTAINED_REGION_MS
+    peak = float(pk["bf16_tflops_sustained"] if sustained else pk["bf16_tflops"])
     achieved = 2.0 * M * N * K / (kern_ms * 1e-3) / 1e12
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak, "peak_source": f"{pk['source']} bf16 dense GEMM, sustained",
+                "frac": achieved / peak,
+                "peak_source": (f"{pk['source']} bf16 dense GEMM, {'sustained' if sustained else 'burst'} "
+                                f"(timed region {ms_total:.0f} ms)"),
                 "frac_of_burst": achieved / float(pk["bf16_tflops"]),
+                "frac_of_sustained": achieved / float(pk["bf16_tflops_sustained"]),
                 "frac_of_nominal_2250": achieved / NOMINAL_FP16_TFLOPS,
                 "kernel": (f"gemm_skinny_f16<{knobs['tile_m']},{knobs['tile_n']},{knobs['stages']}>"
                            if knobs["tile_m"] < 128 else
@@ -516,9 +637,206 @@ def run_ours(args: argparse.Namespace) -> None:
         "config": workload_config(size, world, knobs),
         "pct_of_dense_fp16_peak": 100.0 * value / (NOMINAL_FP16_TFLOPS * world),
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": args.steps,
-        "clocks": clocks, "allgather": allgather,
+        "clocks": clocks, "parity": None if parity is None else parity["ok"], "parity_detail": parity,
+        "allgather": allgather, "shapes": shapes,
     }
     emit(line)
+
+
+def time_exchange(args, A, B, C, step, cfg_id, size, rows, N, world, dev, stream, barrier, checker,
+                  checks) -> Dict[str, object]:
+    """GEMM + all-gather of C, three ways; each timed over the same number of
+    steps (max over ranks), then its last result checked against the oracle."""
+    import torch
+    import torch.distributed as dist
+
+    from infinite_dreams import dispatch, infinite_dreams_ext as ext
+    from infinite_dreams.sharded import release_peer_buffers, sharded_gemm
+
+    Cfull = torch.empty((size, N), device=dev, dtype=torch.float16)
+    n_ag = max(1, min(args.steps, 20))
+
+    def timed(fn) -> float:
+        for _ in range(2):
+            fn()
+        barrier()
+        s0 = torch.cuda.Event(enable_timing=True)
+        s1 = torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for _ in range(n_ag):
+            fn()
+        s1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([s0.elapsed_time(s1)], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t[0]) / n_ag
+
+    def one_shot():
+        step()
+        dist.all_gather_into_tensor(Cfull, C)
+
+    def pipelined():
+        # two row chunks: the first chunk's all-gather overlaps the second chunk's GEMM
+        sharded_gemm(A, B, M_total=size, gather=True, out=Cfull, chunks=2,
+                     compute=lambda a, b, o: ext.gemm_forward_cfg(
+                         a, b, dispatch.lookup(a.shape[0], b.shape[1], a.shape[1]), out=o))
+
+    fused_out = []
+
+    def fused():
+        # every tile goes to all ranks' C from the GEMM's epilogue (NVLink stores), then a
+        # one-element all-reduce on the stream marks all ranks' grids complete
+        fused_out[:] = [sharded_gemm(A, B, M_total=size, gather=True, exchange="fused")]
+
+    def check(name: str, full) -> None:
+        if checker is None:
+            return
+        torch.cuda.synchronize()
+        checks[name] = checker.check_full(full)
+
+    ms_one = timed(one_shot)
+    check("gemm_then_nccl_allgather", Cfull)
+    Cfull.fill_(float("nan"))
+    ms_pipe = timed(pipelined)
+    check("pipelined_2_chunks", Cfull)
+    ms_fused = timed(fused)
+    check("fused_allgather", fused_out[0])
+    fused_out.clear()
+    flop = 2.0 * size ** 3
+    out = {"ms_per_step_gemm_then_allgather": ms_one, "value_gemm_then_allgather": flop / (ms_one * 1e-3) / 1e12,
+           "ms_per_step_pipelined_2_chunks": ms_pipe, "value_pipelined": flop / (ms_pipe * 1e-3) / 1e12,
+           "ms_per_step_fused": ms_fused, "value_fused": flop / (ms_fused * 1e-3) / 1e12,
+           "bytes_received_per_rank": (world - 1) * rows * N * 2, "steps": n_ag,
+           "note": "each rank ends every step with the whole 16384x16384 C; times are max over ranks"}
+    del Cfull
+    release_peer_buffers()
+    return out
+
+
+def time_e2e(args, A, B, cfg_id, size, rows, N, K, world, rank, dev, stream, barrier) -> Dict[str, object]:
+    """End to end through the public op.  Every step each rank copies its own
+    inputs from pinned host memory -- its block of A and its 1/N share of B's
+    rows -- the ranks assemble the full B over NVLink (NCCL all-gather), the
+    GEMM runs, and each rank reads its C block back.  Copies and the gather run
+    on their own streams, so step i+1's upload and step i-1's download overlap
+    step i's GEMM (double-buffered device inputs and outputs)."""
+    import torch
+    import torch.distributed as dist
+
+    from infinite_dreams import infinite_dreams_ext as ext
+
+    kb = K // world
+    hA = [A.cpu().pin_memory() for _ in range(2)]
+    hBs = [B[rank * kb:(rank + 1) * kb].cpu().pin_memory() for _ in range(2)]
+    hC = [torch.empty((rows, N), dtype=torch.float16).pin_memory() for _ in range(2)]
+    dA = [torch.empty_like(A) for _ in range(2)]
+    dB = [torch.empty_like(B) for _ in range(2)]
+    dBs = [dB[b][rank * kb:(rank + 1) * kb] if world == 1 else torch.empty((kb, N), dtype=B.dtype, device=dev)
+           for b in range(2)]
+    dC = [torch.empty((rows, N), dtype=torch.float16, device=dev) for _ in range(2)]
+    s_in = torch.cuda.Stream(dev)
+    s_g = torch.cuda.Stream(dev)
+    s_out = torch.cuda.Stream(dev)
+    # 30 steps amortise the pipeline's fill and drain (one upload and one
+    # download that overlap nothing).
+    e2e_steps = max(2, min(args.steps, 30))
+
+    def run(n_steps: int) -> float:
+        up = [torch.cuda.Event() for _ in range(2)]
+        gathered = [torch.cuda.Event() for _ in range(2)]
+        computed = [torch.cuda.Event() for _ in range(2)]
+        drained = [torch.cuda.Event() for _ in range(2)]
+        start_ev = torch.cuda.Event(enable_timing=True)
+        end_ev = torch.cuda.Event(enable_timing=True)
+        start_ev.record(stream)
+        for s in (s_in, s_g, s_out):
+            s.wait_event(start_ev)
+        for b in range(2):
+            computed[b].record(stream)
+            drained[b].record(s_out)
+            gathered[b].record(s_g)
+        for i in range(n_steps):
+            b = i % 2
+            with torch.cuda.stream(s_in):
+                s_in.wait_event(computed[b])     # dA[b] (and dB[b]) no longer read by step i-2's GEMM
+                s_in.wait_event(gathered[b])     # dBs[b] no longer read by step i-2's gather
+                dA[b].copy_(hA[b], non_blocking=True)
+                dBs[b].copy_(hBs[b], non_blocking=True)
+                up[b].record(s_in)
+            with torch.cuda.stream(s_g):
+                s_g.wait_event(up[b])
+                if world > 1:
+                    dist.all_gather_into_tensor(dB[b], dBs[b])
+                gathered[b].record(s_g)
+            stream.wait_event(gathered[b])
+            stream.wait_event(drained[b])
+            ext.gemm_forward_cfg(dA[b], dB[b], cfg_id, out=dC[b])
+            computed[b].record(stream)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(computed[b])
+                hC[b].copy_(dC[b], non_blocking=True)
+                drained[b].record(s_out)
+        stream.wait_stream(s_out)
+        end_ev.record(stream)
+        torch.cuda.synchronize()
+        return start_ev.elapsed_time(end_ev)
+
+    run(2)
+    barrier()
+    t = torch.tensor([run(e2e_steps)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_e2e = float(t[0]) / e2e_steps
+    out = {"value": 2.0 * size ** 3 / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
+           "h2d_bytes_per_step": (size * K + K * N) * 2, "d2h_bytes_per_step": size * N * 2,
+           "ms_per_step": ms_e2e, "steps": e2e_steps,
+           "path": ("each rank: pinned host A block + 1/N of B's rows -> device (copy stream); NCCL all-gather "
+                    "of B over NVLink (gather stream); infinite_dreams_ext.gemm_forward_cfg; C block -> pinned "
+                    "host (copy stream); uploads/downloads overlap neighbouring steps' GEMMs. Byte counts are "
+                    "whole-job totals over all ranks")}
+    del hA, hBs, hC, dA, dB, dBs, dC
+    return out
+
+
+def shapes_block(args: argparse.Namespace, pk: Dict[str, object]) -> Dict[str, object]:
+    """Every other workload shape through the dispatch table: parity against
+    the oracle, then timing (see infinite_dreams.bench_shapes)."""
+    import torch
+
+    from infinite_dreams import bench_shapes
+    from infinite_dreams.sizes import shape_sets
+
+    sets = [s for s in args.shape_sets.split(",") if s]
+    rows = bench_shapes.run(sets, iters=20, warmup=3, with_torch=True, check=shape_checker(host_threads()),
+                            peaks={"tflops": float(pk["bf16_tflops"]), "gbs": float(pk["hbm_gbs"])})
+    torch.cuda.empty_cache()
+    out: Dict[str, object] = {
+        "timing": ("ms: one launch after an L2 flush (mean of 20 such launches, launch latency included); "
+                   "ms_warm_b2b: back to back through the op on warm caches (the reference tuner's way); "
+                   "ms_graph_b2b: back to back replayed from a CUDA graph; ms_torch_cublas: torch.matmul timed "
+                   "like ms"),
+        "roofline": ("pct_roofline_measured = max(2MNK/bf16 burst peak, 2(MK+KN+MN)/HBM copy rate) / ms, "
+                     "measured peaks of this box"),
+        "rows": [],
+    }
+    keep = ("set", "M", "N", "K", "cfg_id", "knobs", "bound", "ms", "ms_warm_b2b", "ms_graph_b2b",
+            "ms_torch_cublas", "tflops", "gbs", "pct_fp16_peak_nominal", "pct_roofline_nominal",
+            "pct_roofline_measured", "parity")
+    for r in rows:
+        e = {k: r.get(k) for k in keep}
+        e["knobs"] = list(r["knobs"].values())
+        out["rows"].append(e)
+    dflt = [(M, N, K) for (M, N, K) in shape_sets()["default"]]
+    d_rows = [r for r in rows if r["set"] == "default" and (r["M"], r["N"], r["K"]) in dflt]
+    if len(d_rows) == len(dflt):
+        out["default_sizes_mean_ms"] = {
+            "shapes": [f"{M}x{N}x{K}" for (M, N, K) in dflt],
+            "ms_warm_b2b": sum(r["ms_warm_b2b"] for r in d_rows) / len(d_rows),
+            "ms_graph_b2b": sum(r["ms_graph_b2b"] for r in d_rows) / len(d_rows),
+            "ms_cold": sum(r["ms"] for r in d_rows) / len(d_rows),
+            "note": "the reference's published metric: mean kernel ms over its tuner's 5 shapes"}
+    out["parity"] = all(bool(r.get("parity", {}).get("ok")) for r in rows) if rows else None
+    return out
 
 
 def traffic_for(size: int, world: int) -> Optional[float]:

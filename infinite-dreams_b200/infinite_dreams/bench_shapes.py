@@ -22,7 +22,7 @@ import argparse
 import json
 import os
 from pathlib import Path
-from typing import Dict, List, Optional
+from typing import Callable, Dict, List, Optional
 
 NOMINAL_TFLOPS = 2250.0
 NOMINAL_GBS = 8000.0
@@ -85,18 +85,28 @@ def _ops(case, layout: str, epilogue: str, cid: int, out):
 
 
 def run(sets: List[str], iters: int, warmup: int, cfg_override: Optional[int] = None, layout: str = "nn",
-        epilogue: str = "none", with_torch: bool = False) -> List[Dict[str, object]]:
+        epilogue: str = "none", with_torch: bool = False,
+        check: Optional[Callable[..., Dict[str, object]]] = None,
+        peaks: Optional[Dict[str, float]] = None) -> List[Dict[str, object]]:
+    """One row per shape.  ``check(M, N, K, A, B, C)``, when given, is called
+    once on the first result of each shape (before any timing) and its dict
+    is stored under ``"parity"``; ``peaks`` ({"tflops", "gbs"}) overrides the
+    measured-peak denominators."""
     import torch
 
     from . import dispatch, infinite_dreams_ext as ext
     from .tuner import make_bench_cases
     from .utils import time_cuda_ms
 
-    mp = measured_peaks()
+    mp = dict(peaks) if peaks is not None else measured_peaks()
     rows = []
     table = ext.gemm_cfg_table_cpu()
+    seen = set()
     for name in sets:
         for (M, N, K) in _shapes_of(name):
+            if (M, N, K, name) in seen:
+                continue
+            seen.add((M, N, K, name))
             (case,) = make_bench_cases([(M, N, K)], seed=0, dist="skinny" if name == "skinny" else "uniform")
             if cfg_override is None:
                 cid = dispatch.lookup(M, N, K)
@@ -106,6 +116,12 @@ def run(sets: List[str], iters: int, warmup: int, cfg_override: Optional[int] = 
                 cid = cfg_override
             out = torch.zeros((M, N), dtype=torch.float16, device="cuda")
             ours, theirs = _ops(case, layout, epilogue, cid, out)
+            parity = None
+            if check is not None:
+                out.fill_(float("nan"))
+                ours()
+                torch.cuda.synchronize()
+                parity = check(M, N, K, case.A, case.B, out)
             ms = time_cuda_ms(ours, iters=iters, warmup=warmup, flush_l2=True)
             # back-to-back launches on warm caches, the way the reference's
             # tuner timed its kernels (infinite_dreams/utils.py:13-27)
@@ -125,6 +141,8 @@ def run(sets: List[str], iters: int, warmup: int, cfg_override: Optional[int] = 
                 "pct_roofline_measured": 100.0 * roofline_ms(M, N, K, mp["tflops"], mp["gbs"]) / ms,
                 "bound": "tensor" if flops / (NOMINAL_TFLOPS * 1e12) > nbytes / (NOMINAL_GBS * 1e9) else "hbm",
             })
+            if parity is not None:
+                rows[-1]["parity"] = parity
             del case, out
             torch.cuda.empty_cache()
     ext.check_device_errors()

@@ -63,7 +63,8 @@ def test_bench_contract_small(cuda_device):
     """bench.py prints one JSON line with the contract's keys (small size)."""
     env = dict(os.environ, PYTHONPATH=f"{ROOT / 'infinite-dreams_b200'}:{ROOT}")
     r = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--size", "2048", "--steps", "4", "--warmup", "3",
-                        "--no-cpu-baseline"], capture_output=True, text=True, env=env, timeout=600, cwd=ROOT)
+                        "--no-cpu-baseline", "--shape-sets", "single,irregular"],
+                       capture_output=True, text=True, env=env, timeout=600, cwd=ROOT)
     assert r.returncode == 0, r.stderr[-2000:]
     lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
     assert len(lines) == 1
@@ -75,6 +76,12 @@ def test_bench_contract_small(cuda_device):
     assert d["value"] > 50 and np.isfinite(d["roofline"]["frac"])
     assert d["e2e"]["h2d_bytes_per_step"] == 2 * (2048 * 2048 * 2) and d["e2e"]["d2h_bytes_per_step"] == 2048 * 2048 * 2
     assert d["config"]["workload"].startswith("gemm 2048x2048x2048")
+    # outputs checked against the oracle: the GEMM's own C and every shape of the per-shape block
+    assert d["parity"] is True, d["parity_detail"]
+    assert d["shapes"]["parity"] is True and len(d["shapes"]["rows"]) == 5
+    assert all(r["parity"]["ok"] for r in d["shapes"]["rows"])
+    # the clock record is cut to the timed region (here too short for more than a sample or two)
+    assert d["clocks"]["sampler"] in ("nvml", "nvidia-smi") and d["clocks"]["window_ms"] > 0
 
 
 def test_torch_binding_matches_ctypes_path(cuda_device):

@@ -97,3 +97,80 @@ def test_sharded_gemm_nccl_allgather(cuda_device, M):
             assert g.shape == ref.shape and np.isfinite(g).all(), rank
             assert np.abs(g - ref).max() <= tol, ("fused", rank)
         assert len(fused) == (3 if M % world == 0 else 0)
+
+
+def _worker_large(rank, world, port, S, q):
+    """The 16384^3 workload sharded as bench.py shards it; every rank checks
+    sampled rows of both gathered C's (NCCL and fused) against the oracle."""
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parent.parent
+    for p in (str(root), str(root / "infinite-dreams_b200"), str(root / "tests")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    import oracle
+    from infinite_dreams.sharded import broadcast_b, release_peer_buffers, sharded_gemm
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        rows = S // world
+
+        def block(r):
+            g = torch.Generator(device=dev)
+            g.manual_seed(100 + r)
+            return (torch.rand((rows, S), generator=g, device=dev) * 2 - 1).to(torch.float16)
+
+        g = torch.Generator(device=dev)
+        g.manual_seed(99)
+        Bd = (torch.rand((S, S), generator=g, device=dev) * 2 - 1).to(torch.float16) if rank == 0 else \
+            torch.zeros((S, S), dtype=torch.float16, device=dev)
+        broadcast_b(Bd)
+        A_local = block(rank)
+        C = sharded_gemm(A_local, Bd, M_total=S, gather=True)
+        F = sharded_gemm(A_local, Bd, M_total=S, gather=True, exchange="fused")
+        torch.cuda.synchronize()
+        # first, last and two inner rows of every rank's block
+        picks = [r * rows + i for r in range(world) for i in (0, rows // 3, (2 * rows) // 3, rows - 1)]
+        a_rows = torch.cat([block(r)[[i - r * rows for i in picks if r * rows <= i < (r + 1) * rows]]
+                            for r in range(world)], 0)
+        threads = max(1, (os.cpu_count() or 1) // world)
+        ref = oracle.gemm_f16(a_rows.cpu().numpy(), Bd.cpu().numpy(), threads=threads).astype(np.float32)
+        tol = oracle.tolerance(ref, S)
+        got_c = C[picks].float().cpu().numpy()
+        got_f = F[picks].float().cpu().numpy()
+        err_c = float(np.abs(got_c - ref).max()) if np.isfinite(got_c).all() else float("inf")
+        err_f = float(np.abs(got_f - ref).max()) if np.isfinite(got_f).all() else float("inf")
+        q.put((rank, err_c, err_f, tol))
+        del F
+        release_peer_buffers()
+        dist.barrier(device_ids=[rank])
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_16384_cubed_sampled_rows(cuda_device):
+    """The bench workload (16384^3, A row-sharded over every GPU, B replicated): the NCCL all-gather and the
+    fused exchange both give every rank a C whose sampled rows match the oracle."""
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
+        pytest.skip("needs 2 or more GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_large, args=(r, world, port, 16384, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=600) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, err_c, err_f, tol in results:
+        assert err_c <= tol, ("nccl all-gather", rank, err_c, tol)
+        assert err_f <= tol, ("fused exchange", rank, err_f, tol)
