@@ -120,6 +120,7 @@ class ClockSampler:
         self.cuda_index = cuda_index
         self.period = period_s
         self.samples: List[Tuple[float, float, float, List[str]]] = []   # (t, sm MHz, W, reasons)
+        self.bits: List[Tuple[float, int]] = []    # (t, raw NVML clock event reason mask)
         self.max_mhz: Optional[float] = None
         self.source = "none"
         self._stop = threading.Event()
@@ -171,6 +172,7 @@ class ClockSampler:
                 watts = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
                 bits = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(h))
                 self.samples.append((t, mhz, watts, [n for b, n in _REASONS.items() if bits & b]))
+                self.bits.append((t, bits))
             except Exception:
                 return
             self._stop.wait(self.period)
@@ -214,6 +216,9 @@ class ClockSampler:
                "power_w_median": statistics.median(s[2] for s in inside),
                "power_w_max": max(s[2] for s in inside), "sampler": self.source,
                "reason_samples": {r: sum(1 for s in inside if r in s[3]) for r in reasons}}
+        masks = {b for t, b in self.bits if t0 <= t <= t1}
+        if masks:
+            out["reason_masks_seen"] = sorted(hex(b) for b in masks)
         if kernel_ms is not None:
             # clock-normalised kernel time: ms x median MHz (lower is better per clock)
             out["kernel_ms_x_mhz"] = kernel_ms * mhz
