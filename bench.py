@@ -693,6 +693,12 @@ def time_exchange(args, A, B, C, step, cfg_id, size, rows, N, world, dev, stream
         # one-element all-reduce on the stream marks all ranks' grids complete
         fused_out[:] = [sharded_gemm(A, B, M_total=size, gather=True, exchange="fused")]
 
+    copy_out = []
+
+    def fused_copy():
+        # finished chunks of C cross NVLink by the copy engines while the GEMM goes on
+        copy_out[:] = [sharded_gemm(A, B, M_total=size, gather=True, exchange="copy")]
+
     def check(name: str, full) -> None:
         if checker is None:
             return
@@ -707,12 +713,18 @@ def time_exchange(args, A, B, C, step, cfg_id, size, rows, N, world, dev, stream
     ms_fused = timed(fused)
     check("fused_allgather", fused_out[0])
     fused_out.clear()
+    ms_copy = timed(fused_copy)
+    check("copy_engine_allgather", copy_out[0])
+    copy_out.clear()
     flop = 2.0 * size ** 3
     out = {"ms_per_step_gemm_then_allgather": ms_one, "value_gemm_then_allgather": flop / (ms_one * 1e-3) / 1e12,
            "ms_per_step_pipelined_2_chunks": ms_pipe, "value_pipelined": flop / (ms_pipe * 1e-3) / 1e12,
            "ms_per_step_fused": ms_fused, "value_fused": flop / (ms_fused * 1e-3) / 1e12,
+           "ms_per_step_copy_engines": ms_copy, "value_copy_engines": flop / (ms_copy * 1e-3) / 1e12,
            "bytes_received_per_rank": (world - 1) * rows * N * 2, "steps": n_ag,
-           "note": "each rank ends every step with the whole 16384x16384 C; times are max over ranks"}
+           "note": ("each rank ends every step with the whole 16384x16384 C; times are max over ranks. fused: the "
+                    "kernel's epilogue stores every tile into every rank's C over NVLink; copy_engines: the kernel "
+                    "counts finished chunks of C and copy streams waiting on those counts move them")}
     del Cfull
     release_peer_buffers()
     return out

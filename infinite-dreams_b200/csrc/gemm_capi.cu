@@ -12,6 +12,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <algorithm>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -229,6 +230,12 @@ struct OpDesc {
   int act = 0;
   const void* const* peers = nullptr;  // fused all-gather targets (gemm_launch_gather)
   int n_peers = 0;
+  // Copy-engine exchange (gemm_launch_gather_copy): the peers are written by
+  // copies on these streams, not by the kernel.
+  bool copy_exchange = false;
+  void* const* copy_streams = nullptr;
+  int n_copy_streams = 0;
+  unsigned int* chunk_counters = nullptr;
   bool epi() const { return alpha != 1.0f || beta != 0.0f || bias != nullptr || act != 0; }
 };
 
@@ -368,7 +375,7 @@ struct MapCacheEntry {
   bool valid = false;
   CUtensorMap map;
 };
-constexpr int kMapCacheSize = 8;
+constexpr int kMapCacheSize = 32;   // A, B, C and, for the fused all-gather, up to 2 x 7 peer C buffers
 thread_local MapCacheEntry t_map_cache[kMapCacheSize];
 thread_local int t_map_next = 0;
 
@@ -413,6 +420,155 @@ int launch_pack(const void* src, int64_t lds, void* dst, int64_t ldd, int64_t ro
       static_cast<int>(cols));
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? GEMM_OK : fail_cuda(e, "pack_rows_f16 launch");
+}
+
+// ---------------------------------------------------------------- copy-engine exchange
+
+// Chunks of the copy-engine exchange.  The kernel walks tile rows
+// [0, main_rows) column by column, then the tail rows (about one wave of
+// tiles) column by column; the main rows are cut into column chunks that
+// shrink toward the end of the walk, so that the copy of the last main chunk
+// overlaps the tail region's compute, and the tail region is one contiguous
+// block of whole rows.
+static_assert(GEMM_GATHER_COUNTERS == kMaxMainChunks + 1, "one counter per main chunk plus the tail chunk");
+
+struct ExchangePlan {
+  int main_rows = 0, n_main = 0;
+  int bounds[kMaxMainChunks + 1] = {};
+  uint32_t target[kMaxMainChunks + 1] = {};   // epilogue-warp signals per chunk
+};
+
+ExchangePlan exchange_plan(const Plan& pl) {
+  ExchangePlan x;
+  int64_t tail = (pl.workers + pl.tiles_n / 2) / pl.tiles_n;   // rows of one wave of tiles, rounded
+  if (tail < 1) tail = 1;
+  if (tail > pl.tiles_m) tail = pl.tiles_m;
+  x.main_rows = pl.tiles_m - static_cast<int>(tail);
+  if (x.main_rows > 0) {
+    static const double kCut[] = {0.35, 0.65, 0.875, 1.0};
+    x.bounds[0] = 0;
+    for (double f : kCut) {
+      int b = static_cast<int>(f * pl.tiles_n + 0.5);
+      if (b > pl.tiles_n) b = pl.tiles_n;
+      if (b > x.bounds[x.n_main]) x.bounds[++x.n_main] = b;
+    }
+    if (x.bounds[x.n_main] != pl.tiles_n) x.bounds[++x.n_main] = pl.tiles_n;
+  }
+  const uint32_t per_tile = static_cast<uint32_t>(kEpiWarps * pl.cg);
+  for (int c = 0; c < x.n_main; ++c) {
+    x.target[c] = per_tile * static_cast<uint32_t>(x.main_rows * (x.bounds[c + 1] - x.bounds[c]));
+  }
+  x.target[x.n_main] = per_tile * static_cast<uint32_t>(tail * pl.tiles_n);
+  return x;
+}
+
+using WaitValueFn = CUresult (*)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
+
+WaitValueFn wait_value_fn() {
+  static WaitValueFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuStreamWaitValue32", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      return static_cast<WaitValueFn>(nullptr);
+    }
+    return reinterpret_cast<WaitValueFn>(f);
+  }();
+  return fn;
+}
+
+// Events that order the copy streams against the caller's stream, one set
+// per device and host thread (a record followed by its waits is issued
+// without interleaving).
+constexpr int kMaxCopyStreams = 16;
+struct ExchangeEvents {
+  bool ready = false;
+  cudaEvent_t start = nullptr;
+  cudaEvent_t join[kMaxCopyStreams] = {};
+};
+thread_local ExchangeEvents t_xevents[kMaxDevices];
+
+int exchange_events(int dev, ExchangeEvents** out) {
+  ExchangeEvents& ev = t_xevents[dev];
+  if (!ev.ready) {
+    cudaError_t e = cudaEventCreateWithFlags(&ev.start, cudaEventDisableTiming);
+    for (int i = 0; e == cudaSuccess && i < kMaxCopyStreams; ++i) {
+      e = cudaEventCreateWithFlags(&ev.join[i], cudaEventDisableTiming);
+    }
+    if (e != cudaSuccess) return fail_cuda(e, "cudaEventCreateWithFlags");
+    ev.ready = true;
+  }
+  *out = &ev;
+  return GEMM_OK;
+}
+
+// Before the GEMM: reset the chunk counts and start the copy streams after
+// the reset.
+int exchange_begin(const OpDesc& op, int dev, cudaStream_t stream, ExchangeEvents** evs) {
+  int st = exchange_events(dev, evs);
+  if (st != GEMM_OK) return st;
+  cudaError_t e = cudaMemsetAsync(op.chunk_counters, 0, (kMaxMainChunks + 1) * sizeof(unsigned int), stream);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaMemsetAsync(chunk counters)");
+  e = cudaEventRecord((*evs)->start, stream);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaEventRecord");
+  for (int i = 0; i < op.n_copy_streams; ++i) {
+    e = cudaStreamWaitEvent(static_cast<cudaStream_t>(op.copy_streams[i]), (*evs)->start, 0);
+    if (e != cudaSuccess) return fail_cuda(e, "cudaStreamWaitEvent");
+  }
+  return GEMM_OK;
+}
+
+// After the GEMM: on the copy streams, wait (on the GPU) for each chunk's
+// count, copy the chunk into every peer's C, then join the copy streams back
+// into the caller's stream.  Peer k's main chunks go on stream k, its tail
+// chunk on stream n_peers + k (modulo the number of streams), so the tail's
+// copies need not queue behind the last main chunk's.
+int exchange_copies(const OpDesc& op, const Plan& pl, const ExchangePlan& x, const void* C, int64_t M, int64_t N,
+                    int64_t ldc, cudaStream_t stream, ExchangeEvents* evs) {
+  WaitValueFn wait = wait_value_fn();
+  if (!wait) return fail(GEMM_ERR_CUDA, "cuStreamWaitValue32 is not available from the driver");
+  const int64_t bm = static_cast<int64_t>(kBM) * pl.cg;
+  const int S = op.n_copy_streams;
+  for (int c = 0; c <= x.n_main; ++c) {
+    int64_t r0, r1, c0, c1;
+    if (c < x.n_main) {
+      r0 = 0;
+      r1 = std::min<int64_t>(M, x.main_rows * bm);
+      c0 = static_cast<int64_t>(x.bounds[c]) * pl.tile_n;
+      c1 = std::min<int64_t>(N, static_cast<int64_t>(x.bounds[c + 1]) * pl.tile_n);
+    } else {
+      r0 = std::min<int64_t>(M, x.main_rows * bm);
+      r1 = M;
+      c0 = 0;
+      c1 = N;
+    }
+    const CUdeviceptr flag = reinterpret_cast<CUdeviceptr>(op.chunk_counters + c);
+    for (int k = 0; k < op.n_peers; ++k) {
+      cudaStream_t cs = static_cast<cudaStream_t>(op.copy_streams[(c < x.n_main ? k : op.n_peers + k) % S]);
+      CUresult r = wait(reinterpret_cast<CUstream>(cs), flag, x.target[c], CU_STREAM_WAIT_VALUE_GEQ);
+      if (r != CUDA_SUCCESS) {
+        return fail(GEMM_ERR_CUDA, "cuStreamWaitValue32 failed with CUresult " + std::to_string(static_cast<int>(r)));
+      }
+      if (r1 <= r0 || c1 <= c0) continue;
+      const size_t off = static_cast<size_t>(r0 * ldc + c0) * 2;
+      const uint8_t* src = static_cast<const uint8_t*>(C) + off;
+      uint8_t* dst = static_cast<uint8_t*>(const_cast<void*>(op.peers[k])) + off;
+      cudaError_t e;
+      if (c0 == 0 && c1 == ldc) {
+        e = cudaMemcpyAsync(dst, src, static_cast<size_t>((r1 - r0) * ldc) * 2, cudaMemcpyDefault, cs);
+      } else {
+        e = cudaMemcpy2DAsync(dst, static_cast<size_t>(ldc) * 2, src, static_cast<size_t>(ldc) * 2,
+                              static_cast<size_t>(c1 - c0) * 2, static_cast<size_t>(r1 - r0), cudaMemcpyDefault, cs);
+      }
+      if (e != cudaSuccess) return fail_cuda(e, "peer copy");
+    }
+  }
+  for (int i = 0; i < S; ++i) {
+    cudaError_t e = cudaEventRecord(evs->join[i], static_cast<cudaStream_t>(op.copy_streams[i]));
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(stream, evs->join[i], 0);
+    if (e != cudaSuccess) return fail_cuda(e, "joining the copy streams");
+  }
+  return GEMM_OK;
 }
 
 int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
@@ -476,13 +632,40 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
   p.D = op.beta != 0.0f ? static_cast<const __half*>(op.D) : nullptr;
   p.ldd = op.beta != 0.0f ? op.ldd : 0;
   p.bias = static_cast<const __half*>(op.bias);
-  p.n_peers = op.n_peers;
+  // copy-engine exchange: the kernel writes only its own C
+  p.n_peers = op.copy_exchange ? 0 : op.n_peers;
+  p.peer_tma = 0;
+  p.xwalk = 0;
+  p.main_rows = 0;
+  p.n_main = 0;
+  std::memset(p.col_bounds, 0, sizeof(p.col_bounds));
+  p.chunk_done = nullptr;
   for (int i = 0; i < kMaxPeers; ++i) {
     p.peer_C[i] = i < op.n_peers ? static_cast<__half*>(const_cast<void*>(op.peers[i])) : nullptr;
   }
+  std::memset(p.peer_map, 0, sizeof(p.peer_map));
   if (op.n_peers > 0 && (pl.skinny || pl.max_parts > 1 || K == 0)) {
     return fail(GEMM_ERR_UNSUPPORTED, "the fused all-gather needs K > 0 and a configuration without split-K / "
                                       "stream-K and with tile_m >= 128");
+  }
+  if (op.copy_exchange) {
+    if (pl.skinny || pl.max_parts > 1 || K == 0 || op.epi() || op.trans_a || op.trans_b) {
+      return fail(GEMM_ERR_UNSUPPORTED, "the copy-engine exchange needs K > 0, row-major operands, no fused "
+                                        "epilogue and a configuration without split-K / stream-K with tile_m >= 128");
+    }
+    if (!op.copy_streams || op.n_copy_streams < 1 || op.n_copy_streams > kMaxCopyStreams) {
+      return fail(GEMM_ERR_INVALID_ARG, "the copy-engine exchange needs 1 to " + std::to_string(kMaxCopyStreams) +
+                                            " copy streams");
+    }
+    for (int i = 0; i < op.n_copy_streams; ++i) {
+      if (!op.copy_streams[i] || op.copy_streams[i] == stream_v) {
+        return fail(GEMM_ERR_INVALID_ARG, "copy streams must be created streams, other than the launch stream");
+      }
+    }
+    if (!op.chunk_counters || reinterpret_cast<uintptr_t>(op.chunk_counters) % 4u) {
+      return fail(GEMM_ERR_INVALID_ARG, "chunk_counters must be a 4-byte aligned device array of "
+                                        "GEMM_GATHER_COUNTERS unsigned ints");
+    }
   }
   if (K == 0) {
     // Empty reduction: C = 0 (the reference kernel's loop body never runs),
@@ -601,6 +784,17 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
   if (c_tma) {
     st = encode_2d_cached(&tmC, C, N, M, ldc, kStoreCols, kStoreRows, "C");
     if (st != GEMM_OK) return st;
+    // Fused all-gather: each peer's copy of C gets the same map at its own
+    // address, so every staged box goes there by one TMA store.
+    bool peers_tma = p.n_peers > 0;
+    for (int i = 0; i < p.n_peers; ++i) peers_tma = peers_tma && tma_addressable(op.peers[i], ldc);
+    if (peers_tma) {
+      for (int i = 0; i < p.n_peers; ++i) {
+        st = encode_2d_cached(&p.peer_map[i], op.peers[i], N, M, ldc, kStoreCols, kStoreRows, "peer C");
+        if (st != GEMM_OK) return st;
+      }
+      p.peer_tma = 1;
+    }
   }
 
   p.tiles_m = pl.tiles_m;
@@ -618,10 +812,24 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
   p.partials = pl.max_parts > 1 ? reinterpret_cast<float*>(wsb + pl.off_partials) : nullptr;
   p.counters = pl.max_parts > 1 ? reinterpret_cast<unsigned int*>(wsb) : nullptr;
 
+  ExchangePlan xp;
+  ExchangeEvents* xev = nullptr;
+  if (op.copy_exchange) {
+    xp = exchange_plan(pl);
+    p.xwalk = 1;
+    p.main_rows = xp.main_rows;
+    p.n_main = xp.n_main;
+    std::memcpy(p.col_bounds, xp.bounds, sizeof(p.col_bounds));
+    p.chunk_done = op.chunk_counters;
+    st = exchange_begin(op, dev, stream, &xev);
+    if (st != GEMM_OK) return st;
+  }
+
   // persistent grid: one CTA (or CTA pair) per SM (pair), at most one per work unit
   const int grid = pl.workers * pl.cg;
   e = var->fn(tmA, tmB, tmC, p, grid, stream);
   if (e != cudaSuccess) return fail_cuda(e, "gemm kernel launch");
+  if (op.copy_exchange) return exchange_copies(op, pl, xp, C, M, N, ldc, stream, xev);
   return GEMM_OK;
 }
 
@@ -727,6 +935,21 @@ int gemm_launch_gather(const void* A, const void* B, void* C, int64_t M, int64_t
   OpDesc op;
   op.peers = peer_C;
   op.n_peers = n_peers;
+  return launch_impl(A, B, C, M, N, K, lda, ldb, ldc, op, cfg_id, workspace, workspace_bytes, stream);
+}
+
+int gemm_launch_gather_copy(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                            int64_t ldb, int64_t ldc, const void* const* peer_C, int n_peers, int cfg_id,
+                            void* workspace, size_t workspace_bytes, void* stream, void* const* copy_streams,
+                            int n_copy_streams, unsigned int* chunk_counters) {
+  t_last_error.clear();
+  OpDesc op;
+  op.peers = peer_C;
+  op.n_peers = n_peers;
+  op.copy_exchange = true;
+  op.copy_streams = copy_streams;
+  op.n_copy_streams = n_copy_streams;
+  op.chunk_counters = chunk_counters;
   return launch_impl(A, B, C, M, N, K, lda, ldb, ldc, op, cfg_id, workspace, workspace_bytes, stream);
 }
 

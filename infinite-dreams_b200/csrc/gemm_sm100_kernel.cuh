@@ -51,6 +51,7 @@ constexpr int kStoreRows = 32;    // rows per epilogue store box (one warp's TME
 constexpr int kStoreCols = 64;    // columns per epilogue store box (128 bytes)
 constexpr int kCounterSlots = 65536;  // split-K tile tickets at the head of the workspace
 constexpr int kMaxPeers = 7;          // peer copies of C (fused all-gather over 8 GPUs)
+constexpr int kMaxMainChunks = 8;     // column chunks of the copy-engine exchange's main region
 
 struct GemmParams {
   int M, N, K;
@@ -87,8 +88,27 @@ struct GemmParams {
   // Fused all-gather: each finished box of C is also stored into the C of
   // every peer GPU (peer_C[i]: that GPU's copy at this rank's offset, same
   // pitch ldc), over NVLink, right after it is staged.  Non-split configs.
+  // peer_tma = 1 (C TMA-addressable): the staged box goes to each peer by a
+  // TMA store through peer_map[i] (peer_C[i] with C's extents, pitch and
+  // box), issued next to the local store; the TMA unit moves the bytes and
+  // the epilogue warp only waits for its staging buffer to be read.
+  // peer_tma = 0: the warp copies the box with 16-byte stores.
   int n_peers;
+  int peer_tma;
   __half* peer_C[kMaxPeers];
+  CUtensorMap peer_map[kMaxPeers];
+  // Copy-engine exchange (gemm_launch_gather_copy).  xwalk = 1 walks the
+  // tiles in two regions, each column by column (M fastest): the tile rows
+  // [0, main_rows), then the rest (the tail region, about one wave of
+  // tiles).  Once every box of a tile has landed in C, each epilogue warp
+  // adds 1 to chunk_done[chunk of the tile]: chunk c < n_main is the main
+  // rows' tile columns [col_bounds[c], col_bounds[c + 1]); chunk n_main is
+  // the tail region (whole rows, so one contiguous block of C).  Copy
+  // streams wait on these counts (on the GPU) and then move each chunk to
+  // the peers with the copy engines, while the GEMM goes on.
+  int xwalk, main_rows, n_main;
+  int col_bounds[kMaxMainChunks + 1];
+  unsigned int* chunk_done;
 };
 
 template <int BN, int STAGES, int CG>
@@ -127,8 +147,22 @@ struct SmemPlan {
   static_assert(kOffB % 1024 == 0 && kOffC % 1024 == 0, "swizzled buffers need 1024-byte alignment");
 };
 
-// Tile index -> (tile row, tile column) in grouped raster order.
+// Tile index -> (tile row, tile column) in grouped raster order (or the
+// copy-engine exchange's two-region walk).
 __device__ __forceinline__ void tile_coords(const GemmParams& p, int t, int& tm, int& tn) {
+  if (p.xwalk) {
+    const int main_tiles = p.main_rows * p.tiles_n;
+    if (t < main_tiles) {
+      tm = t % p.main_rows;
+      tn = t / p.main_rows;
+    } else {
+      const int tail = p.tiles_m - p.main_rows;
+      const int u = t - main_tiles;
+      tm = p.main_rows + u % tail;
+      tn = u / tail;
+    }
+    return;
+  }
   if (p.raster == 0) {
     const int per_group = p.group * p.tiles_n;
     const int g = t / per_group;
@@ -146,6 +180,14 @@ __device__ __forceinline__ void tile_coords(const GemmParams& p, int t, int& tm,
     tn = first + r % gs;
     tm = r / gs;
   }
+}
+
+// Chunk of the copy-engine exchange that tile (tm, tn) belongs to.
+__device__ __forceinline__ int exchange_chunk(const GemmParams& p, int tm, int tn) {
+  if (tm >= p.main_rows) return p.n_main;
+  int c = 0;
+  while (c + 1 < p.n_main && tn >= p.col_bounds[c + 1]) ++c;
+  return c;
 }
 
 // One piece of work: tile (tm, tn), K blocks [kb0, kb1), and which of the
@@ -467,7 +509,7 @@ __device__ __forceinline__ void stage_row_sw128(uint8_t* buf, int lane, const fl
 template <int BN, int STAGES, int CG>
 __global__ void __launch_bounds__(kNumThreads, 1)
     gemm_f16_sm100(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
+                   const __grid_constant__ CUtensorMap tmC, const __grid_constant__ GemmParams p) {
   using Plan = SmemPlan<BN, STAGES, CG>;
   constexpr int kBNc = Plan::kBNc;
   extern __shared__ uint8_t smem_raw[];
@@ -519,6 +561,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
     if (p.c_tma) prefetch_tmap(&tmC);
+    if (p.peer_tma) {
+      for (int q = 0; q < p.n_peers; ++q) prefetch_tmap(&p.peer_map[q]);
+    }
   }
   if (warp < 2 && lane == 0) first_have = work_next(p, cluster_id, num_clusters, first_wi, first_w);
   if (warp == 1) {
@@ -888,7 +933,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
               // A box that starts past the edge has nothing to write; skip it
               // but still close a (possibly empty) bulk group so that the
               // wait_group.read<1> accounting above stays per buffer.
-              if (row0 < p.M && col0 < p.N) tma_store_2d(&tmC, buf, col0, row0);
+              if (row0 < p.M && col0 < p.N) {
+                tma_store_2d(&tmC, buf, col0, row0);
+                if (p.peer_tma) {
+                  for (int q = 0; q < p.n_peers; ++q) tma_store_2d(&p.peer_map[q], buf, col0, row0);
+                }
+              }
               bulk_commit_group();
             }
           } else {
@@ -909,7 +959,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             }
             __syncwarp();
           }
-          if (p.n_peers > 0) {
+          if (p.n_peers > 0 && !p.peer_tma) {
             __syncwarp();  // every lane's row is staged
             copy_box_to_peers(p, buf, row0, col0, lane);
             __syncwarp();
@@ -927,6 +977,15 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) release_acc(kHalvesEpi ? 1 : acc);
+      if (p.chunk_done != nullptr) {
+        // Every box of this warp's part of the tile is in C (TMA stores
+        // complete, plain stores fenced) before the chunk's count moves.
+        if (lane == 0 && p.c_tma) bulk_wait_group<0>();
+        fence_proxy_async_global();
+        __threadfence_system();
+        __syncwarp();
+        if (lane == 0) atomicAdd_system(&p.chunk_done[exchange_chunk(p, tm, tn)], 1u);
+      }
       if (++acc == Plan::kNumAcc) {
         acc = 0;
         acc_phase ^= 1u;
@@ -935,13 +994,30 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     if (!ok) {
       *abort_flag = 1;
       atomicOr(p.err, kDevErrTimeoutEpilogue);
+      // The copy streams wait on the chunk counts: release them all (the
+      // copies then move whatever is in C, and the error word reports the
+      // timeout), so no stream is left waiting on this grid.
+      if (p.chunk_done != nullptr && threadIdx.x == 64) {
+        for (int c = 0; c <= p.n_main; ++c) atomicMax(&p.chunk_done[c], 0x3fffffffu);
+      }
     }
     // The staging smem must stay valid until the last TMA stores have read it;
     // their global writes complete with the grid.
-    if (p.c_tma && lane == 0) bulk_wait_group_read<0>();
+    if (p.c_tma && lane == 0) {
+      // With peers, wait for the stores themselves (not only their reads of
+      // shared memory): every byte has reached its GPU before the fence below.
+      if (p.n_peers > 0) {
+        bulk_wait_group<0>();
+      } else {
+        bulk_wait_group_read<0>();
+      }
+    }
     // Peer stores are ordered before anything this thread does later (the
     // grid's completion, which the ranks then agree on through NCCL).
-    if (p.n_peers > 0) __threadfence_system();
+    if (p.n_peers > 0) {
+      __syncwarp();
+      __threadfence_system();
+    }
   }
 
   // ------------------------------------------------------------ teardown

@@ -202,6 +202,20 @@ __device__ __forceinline__ void bulk_wait_group_read() {
   asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
 }
 
+// Waits until at most N bulk groups of this thread are pending, counting a
+// group as pending until its writes are complete (not only its reads of
+// shared memory, as above).
+template <int N>
+__device__ __forceinline__ void bulk_wait_group() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Orders this thread's async-proxy accesses of global memory (completed
+// TMA stores) with its later generic-proxy accesses.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // Make generic-proxy writes to shared memory visible to the async proxy
 // (TMA store / tcgen05.mma operand reads).
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -20,6 +20,15 @@ the remaining tiles' mainloop.  A one-element NCCL all-reduce issued after
 the launch on the same stream marks the point where every rank's grid, and
 with it every write into this rank's C, has completed.  No kernel reads
 another GPU's memory; peers are only written to.
+
+``exchange="copy"`` uses the same buffers, but the bytes cross NVLink by the
+copy engines (``gemm_launch_gather_copy``): the kernel finishes C in chunks
+and counts finished tiles per chunk, and per-peer copy streams wait on the
+GPU for each chunk's count before copying it into the peers' C.  Remote
+stores from the SMs share their path to memory with the GEMM's own operand
+loads; when the links are busy the loads queue behind them.  The copy
+engines take that traffic off the SMs, so the GEMM runs at its own speed
+while the exchange proceeds.
 """
 from __future__ import annotations
 
@@ -63,17 +72,18 @@ def sharded_gemm(A_local: torch.Tensor, B: torch.Tensor, M_total: Optional[int] 
     kernel-bank GEMM.  ``chunks`` > 1 overlaps the all-gather with the
     compute (equal row blocks only; other cases fall back to one exchange).
     ``exchange="fused"`` (gather=True, CUDA, equal row blocks) writes every
-    tile to all ranks from inside the GEMM; the returned full C is a buffer
-    owned by this module: it stays intact until the second fused call of
-    that shape after this one, provided whatever reads it is issued on the
-    calling stream before the next fused call.
+    tile to all ranks from inside the GEMM; ``exchange="copy"`` moves the
+    finished chunks of C with the copy engines while the GEMM runs.  In both
+    the returned full C is a buffer owned by this module: it stays intact
+    until the second such call of that shape after this one, provided
+    whatever reads it is issued on the calling stream before the next call.
     """
-    if exchange not in ("nccl", "fused"):
-        raise ValueError("exchange must be 'nccl' or 'fused'")
-    if exchange == "fused" and gather and dist.is_initialized() and dist.get_world_size(group) > 1:
+    if exchange not in ("nccl", "fused", "copy"):
+        raise ValueError("exchange must be 'nccl', 'fused' or 'copy'")
+    if exchange in ("fused", "copy") and gather and dist.is_initialized() and dist.get_world_size(group) > 1:
         if out is not None or compute is not None:
-            raise ValueError("exchange='fused' owns its output buffer and runs the kernel bank itself")
-        return _fused_gather(A_local, B, M_total, group)
+            raise ValueError(f"exchange='{exchange}' owns its output buffer and runs the kernel bank itself")
+        return _fused_gather(A_local, B, M_total, group, copy_engines=(exchange == "copy"))
     compute = compute or _default_compute
     if gather and chunks > 1 and dist.is_initialized() and dist.get_world_size(group) > 1:
         full = _pipelined_gather(A_local, B, M_total, group, out, compute, chunks)
@@ -232,7 +242,26 @@ def _gather_cfg(rows: int, N: int, K: int) -> int:
     return _capi.cfg_find(fallback)
 
 
-def _fused_gather(A_local: torch.Tensor, B: torch.Tensor, M_total: Optional[int], group) -> torch.Tensor:
+_copy_res: Dict[int, Tuple[List[torch.cuda.Stream], torch.Tensor]] = {}
+
+
+def _copy_resources(device: torch.device, n_peers: int) -> Tuple[List[torch.cuda.Stream], torch.Tensor]:
+    """Per device: 2 * n_peers copy streams (a peer's last chunk gets a
+    stream of its own) and the chunk counters of the copy-engine exchange."""
+    from . import _capi
+
+    with _ipc_lock:
+        res = _copy_res.get(device.index)
+        if res is None or len(res[0]) < 2 * n_peers:
+            streams = [torch.cuda.Stream(device) for _ in range(2 * n_peers)]
+            counters = torch.zeros(_capi.GEMM_GATHER_COUNTERS, dtype=torch.int32, device=device)
+            res = (streams, counters)
+            _copy_res[device.index] = res
+    return res
+
+
+def _fused_gather(A_local: torch.Tensor, B: torch.Tensor, M_total: Optional[int], group,
+                  copy_engines: bool = False) -> torch.Tensor:
     from . import _capi, infinite_dreams_ext as ext
 
     if not (A_local.is_cuda and B.is_cuda):
@@ -255,9 +284,17 @@ def _fused_gather(A_local: torch.Tensor, B: torch.Tensor, M_total: Optional[int]
         stream = torch.cuda.current_stream(device)
         need = _capi.lib.gemm_workspace_bytes(A_local.data_ptr(), B.data_ptr(), rows, N, K, K, N, cid)
         ws_ptr, ws_len = ext._workspace(device, stream, need) if need else (0, 0)
-        _capi.check(_capi.lib.gemm_launch_gather(A_local.data_ptr(), B.data_ptr(), mine.data_ptr(), rows, N, K, K, N,
-                                                 N, arr, len(targets), cid, ws_ptr or None, ws_len,
-                                                 stream.cuda_stream or None), "gemm_launch_gather")
+        if copy_engines:
+            streams, counters = _copy_resources(device, len(targets))
+            carr = (ctypes.c_void_p * len(streams))(*[s.cuda_stream for s in streams])
+            _capi.check(_capi.lib.gemm_launch_gather_copy(
+                A_local.data_ptr(), B.data_ptr(), mine.data_ptr(), rows, N, K, K, N, N, arr, len(targets), cid,
+                ws_ptr or None, ws_len, stream.cuda_stream or None, carr, len(streams), counters.data_ptr()),
+                "gemm_launch_gather_copy")
+        else:
+            _capi.check(_capi.lib.gemm_launch_gather(A_local.data_ptr(), B.data_ptr(), mine.data_ptr(), rows, N, K, K,
+                                                     N, N, arr, len(targets), cid, ws_ptr or None, ws_len,
+                                                     stream.cuda_stream or None), "gemm_launch_gather")
         # Ordered after this rank's grid on its stream: completes once every
         # rank's grid (and so every write into this rank's C) has finished.
         done = torch.zeros(1, dtype=torch.float32, device=device)
