@@ -49,8 +49,8 @@ def _worker(rank, world, port, M, N, K, q):
         if M % world == 0:
             # tiles written into every rank's C over NVLink by the GEMM itself; three calls, so that
             # one of the two alternating buffers is reused after being overwritten with NaN
-            for _ in range(3):
-                F = sharded_gemm(A_local, Bd, M_total=M, gather=True, exchange="fused")
+            for exchange in ("fused", "fused", "fused", "copy", "copy", "copy"):
+                F = sharded_gemm(A_local, Bd, M_total=M, gather=True, exchange=exchange)
                 torch.cuda.synchronize()
                 fused.append(F.cpu().numpy().view(np.uint16).copy())
                 F.fill_(float("nan"))   # the next call must rewrite every element
@@ -96,7 +96,7 @@ def test_sharded_gemm_nccl_allgather(cuda_device, M):
             g = f.view(np.float16).astype(np.float32)
             assert g.shape == ref.shape and np.isfinite(g).all(), rank
             assert np.abs(g - ref).max() <= tol, ("fused", rank)
-        assert len(fused) == (3 if M % world == 0 else 0)
+        assert len(fused) == (6 if M % world == 0 else 0)
 
 
 def _worker_large(rank, world, port, S, q):
@@ -136,6 +136,8 @@ def _worker_large(rank, world, port, S, q):
         C = sharded_gemm(A_local, Bd, M_total=S, gather=True)
         F = sharded_gemm(A_local, Bd, M_total=S, gather=True, exchange="fused")
         torch.cuda.synchronize()
+        G = sharded_gemm(A_local, Bd, M_total=S, gather=True, exchange="copy")
+        torch.cuda.synchronize()
         # first, last and two inner rows of every rank's block
         picks = [r * rows + i for r in range(world) for i in (0, rows // 3, (2 * rows) // 3, rows - 1)]
         a_rows = torch.cat([block(r)[[i - r * rows for i in picks if r * rows <= i < (r + 1) * rows]]
@@ -147,8 +149,10 @@ def _worker_large(rank, world, port, S, q):
         got_f = F[picks].float().cpu().numpy()
         err_c = float(np.abs(got_c - ref).max()) if np.isfinite(got_c).all() else float("inf")
         err_f = float(np.abs(got_f - ref).max()) if np.isfinite(got_f).all() else float("inf")
-        q.put((rank, err_c, err_f, tol))
-        del F
+        got_g = G[picks].float().cpu().numpy()
+        err_g = float(np.abs(got_g - ref).max()) if np.isfinite(got_g).all() else float("inf")
+        q.put((rank, err_c, max(err_f, err_g), tol))
+        del F, G
         release_peer_buffers()
         dist.barrier(device_ids=[rank])
     finally:
@@ -156,8 +160,8 @@ def _worker_large(rank, world, port, S, q):
 
 
 def test_sharded_16384_cubed_sampled_rows(cuda_device):
-    """The bench workload (16384^3, A row-sharded over every GPU, B replicated): the NCCL all-gather and the
-    fused exchange both give every rank a C whose sampled rows match the oracle."""
+    """The bench workload (16384^3, A row-sharded over every GPU, B replicated): the NCCL all-gather, the
+    fused exchange and the copy-engine exchange all give every rank a C whose sampled rows match the oracle."""
     world = min(torch.cuda.device_count(), 8)
     if world < 2:
         pytest.skip("needs 2 or more GPUs")
@@ -173,4 +177,4 @@ def test_sharded_16384_cubed_sampled_rows(cuda_device):
         assert p.exitcode == 0
     for rank, err_c, err_f, tol in results:
         assert err_c <= tol, ("nccl all-gather", rank, err_c, tol)
-        assert err_f <= tol, ("fused exchange", rank, err_f, tol)
+        assert err_f <= tol, ("fused and copy-engine exchanges", rank, err_f, tol)
