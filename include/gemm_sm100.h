@@ -142,21 +142,21 @@ int gemm_launch_gather(const void* A, const void* B, void* C, int64_t M, int64_t
                        void* workspace, size_t workspace_bytes, void* stream);
 
 /* gemm_launch_gather with the transfer done by the copy engines instead of
- * the kernel's own stores.  The kernel walks the tiles in an order that
- * finishes C in chunks (column strips of the first tile rows, then the last
- * tile rows as one contiguous block), counts finished tiles per chunk in
- * chunk_counters (device memory of GEMM_GATHER_COUNTERS unsigned ints,
- * caller-owned, not shared by concurrent calls; reset here on `stream`), and
- * every copy stream waits on the GPU for a chunk's count before copying the
- * chunk into the peers' C -- so the copies overlap the rest of the GEMM and
- * the SMs issue no remote stores.  copy_streams[0..n_copy_streams) are
- * created streams other than `stream` (2 * n_peers lets the last chunk's
- * copies run beside the previous one's); on return they are joined back into
- * `stream`, so work queued on `stream` afterwards (the closing collective)
- * follows every copy of this rank.  Same restrictions as gemm_launch_gather,
- * plus row-major operands and no fused epilogue.  Extends the reference,
- * which ran on one GPU. */
-#define GEMM_GATHER_COUNTERS 9
+ * the kernel's own stores.  The kernel finishes C in bands of whole rows (at
+ * most GEMM_GATHER_COUNTERS of them, walked in order), counts finished tiles
+ * per band in chunk_counters (device memory of GEMM_GATHER_COUNTERS
+ * unsigned ints, caller-owned, not shared by concurrent calls; reset here
+ * on `stream`), and copy streams wait on the GPU for a band's count before
+ * copying the band -- one contiguous block -- into the peers' C.  The copies
+ * overlap the rest of the GEMM and the SMs issue no remote stores.
+ * copy_streams[0..n_copy_streams) are created streams other than `stream`
+ * (2 * n_peers lets consecutive bands' copies overlap); on return they are
+ * joined back into `stream`, so work queued on `stream` afterwards (the
+ * closing collective) follows every copy of this rank.  The configuration's
+ * raster and group are replaced by the band walk.  Same restrictions as
+ * gemm_launch_gather, plus row-major operands and no fused epilogue.
+ * Extends the reference, which ran on one GPU. */
+#define GEMM_GATHER_COUNTERS 16
 int gemm_launch_gather_copy(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
                             int64_t ldb, int64_t ldc, const void* const* peer_C, int n_peers, int cfg_id,
                             void* workspace, size_t workspace_bytes, void* stream, void* const* copy_streams,

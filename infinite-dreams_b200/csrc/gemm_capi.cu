@@ -424,41 +424,28 @@ int launch_pack(const void* src, int64_t lds, void* dst, int64_t ldd, int64_t ro
 
 // ---------------------------------------------------------------- copy-engine exchange
 
-// Chunks of the copy-engine exchange.  The kernel walks tile rows
-// [0, main_rows) column by column, then the tail rows (about one wave of
-// tiles) column by column; the main rows are cut into column chunks that
-// shrink toward the end of the walk, so that the copy of the last main chunk
-// overlaps the tail region's compute, and the tail region is one contiguous
-// block of whole rows.
-static_assert(GEMM_GATHER_COUNTERS == kMaxMainChunks + 1, "one counter per main chunk plus the tail chunk");
+// Chunks of the copy-engine exchange: bands of whole tile rows, at most
+// kMaxChunks of them, walked in order (raster 0 with group = rows per band,
+// so the tiles of a band are walked column by column and share their B
+// panels in L2).  A band is a contiguous block of C: its copies run at the
+// copy engines' full rate, and the last band -- the part of the exchange
+// that cannot overlap the GEMM -- is at most 1/kMaxChunks of C.
+static_assert(GEMM_GATHER_COUNTERS == kMaxChunks, "one counter per row-band chunk");
 
 struct ExchangePlan {
-  int main_rows = 0, n_main = 0;
-  int bounds[kMaxMainChunks + 1] = {};
-  uint32_t target[kMaxMainChunks + 1] = {};   // epilogue-warp signals per chunk
+  int chunk_rows = 1, n_chunks = 0;
+  uint32_t target[kMaxChunks] = {};   // epilogue-warp signals per chunk
 };
 
 ExchangePlan exchange_plan(const Plan& pl) {
   ExchangePlan x;
-  int64_t tail = (pl.workers + pl.tiles_n / 2) / pl.tiles_n;   // rows of one wave of tiles, rounded
-  if (tail < 1) tail = 1;
-  if (tail > pl.tiles_m) tail = pl.tiles_m;
-  x.main_rows = pl.tiles_m - static_cast<int>(tail);
-  if (x.main_rows > 0) {
-    static const double kCut[] = {0.35, 0.65, 0.875, 1.0};
-    x.bounds[0] = 0;
-    for (double f : kCut) {
-      int b = static_cast<int>(f * pl.tiles_n + 0.5);
-      if (b > pl.tiles_n) b = pl.tiles_n;
-      if (b > x.bounds[x.n_main]) x.bounds[++x.n_main] = b;
-    }
-    if (x.bounds[x.n_main] != pl.tiles_n) x.bounds[++x.n_main] = pl.tiles_n;
-  }
+  x.chunk_rows = (pl.tiles_m + kMaxChunks - 1) / kMaxChunks;
+  x.n_chunks = (pl.tiles_m + x.chunk_rows - 1) / x.chunk_rows;
   const uint32_t per_tile = static_cast<uint32_t>(kEpiWarps * pl.cg);
-  for (int c = 0; c < x.n_main; ++c) {
-    x.target[c] = per_tile * static_cast<uint32_t>(x.main_rows * (x.bounds[c + 1] - x.bounds[c]));
+  for (int c = 0; c < x.n_chunks; ++c) {
+    const int rows = std::min(pl.tiles_m, (c + 1) * x.chunk_rows) - c * x.chunk_rows;
+    x.target[c] = per_tile * static_cast<uint32_t>(rows * pl.tiles_n);
   }
-  x.target[x.n_main] = per_tile * static_cast<uint32_t>(tail * pl.tiles_n);
   return x;
 }
 
@@ -507,7 +494,7 @@ int exchange_events(int dev, ExchangeEvents** out) {
 int exchange_begin(const OpDesc& op, int dev, cudaStream_t stream, ExchangeEvents** evs) {
   int st = exchange_events(dev, evs);
   if (st != GEMM_OK) return st;
-  cudaError_t e = cudaMemsetAsync(op.chunk_counters, 0, (kMaxMainChunks + 1) * sizeof(unsigned int), stream);
+  cudaError_t e = cudaMemsetAsync(op.chunk_counters, 0, kMaxChunks * sizeof(unsigned int), stream);
   if (e != cudaSuccess) return fail_cuda(e, "cudaMemsetAsync(chunk counters)");
   e = cudaEventRecord((*evs)->start, stream);
   if (e != cudaSuccess) return fail_cuda(e, "cudaEventRecord");
@@ -518,47 +505,36 @@ int exchange_begin(const OpDesc& op, int dev, cudaStream_t stream, ExchangeEvent
   return GEMM_OK;
 }
 
-// After the GEMM: on the copy streams, wait (on the GPU) for each chunk's
-// count, copy the chunk into every peer's C, then join the copy streams back
-// into the caller's stream.  Peer k's main chunks go on stream k, its tail
-// chunk on stream n_peers + k (modulo the number of streams), so the tail's
-// copies need not queue behind the last main chunk's.
+// After the GEMM: on the copy streams, wait (on the GPU) for each band's
+// count, copy the band into every peer's C, then join the copy streams back
+// into the caller's stream.  Bands alternate between two sets of streams
+// (peer k: stream k, then stream n_peers + k, modulo the number of streams),
+// so a band's copies need not queue behind the previous band's.
 int exchange_copies(const OpDesc& op, const Plan& pl, const ExchangePlan& x, const void* C, int64_t M, int64_t N,
                     int64_t ldc, cudaStream_t stream, ExchangeEvents* evs) {
   WaitValueFn wait = wait_value_fn();
   if (!wait) return fail(GEMM_ERR_CUDA, "cuStreamWaitValue32 is not available from the driver");
-  const int64_t bm = static_cast<int64_t>(kBM) * pl.cg;
+  const int64_t bm = static_cast<int64_t>(kBM) * pl.cg * x.chunk_rows;
   const int S = op.n_copy_streams;
-  for (int c = 0; c <= x.n_main; ++c) {
-    int64_t r0, r1, c0, c1;
-    if (c < x.n_main) {
-      r0 = 0;
-      r1 = std::min<int64_t>(M, x.main_rows * bm);
-      c0 = static_cast<int64_t>(x.bounds[c]) * pl.tile_n;
-      c1 = std::min<int64_t>(N, static_cast<int64_t>(x.bounds[c + 1]) * pl.tile_n);
-    } else {
-      r0 = std::min<int64_t>(M, x.main_rows * bm);
-      r1 = M;
-      c0 = 0;
-      c1 = N;
-    }
+  for (int c = 0; c < x.n_chunks; ++c) {
+    const int64_t r0 = std::min<int64_t>(M, c * bm), r1 = std::min<int64_t>(M, (c + 1) * bm);
     const CUdeviceptr flag = reinterpret_cast<CUdeviceptr>(op.chunk_counters + c);
     for (int k = 0; k < op.n_peers; ++k) {
-      cudaStream_t cs = static_cast<cudaStream_t>(op.copy_streams[(c < x.n_main ? k : op.n_peers + k) % S]);
+      cudaStream_t cs = static_cast<cudaStream_t>(op.copy_streams[(k + (c % 2) * op.n_peers) % S]);
       CUresult r = wait(reinterpret_cast<CUstream>(cs), flag, x.target[c], CU_STREAM_WAIT_VALUE_GEQ);
       if (r != CUDA_SUCCESS) {
         return fail(GEMM_ERR_CUDA, "cuStreamWaitValue32 failed with CUresult " + std::to_string(static_cast<int>(r)));
       }
-      if (r1 <= r0 || c1 <= c0) continue;
-      const size_t off = static_cast<size_t>(r0 * ldc + c0) * 2;
+      if (r1 <= r0) continue;
+      const size_t off = static_cast<size_t>(r0 * ldc) * 2;
       const uint8_t* src = static_cast<const uint8_t*>(C) + off;
       uint8_t* dst = static_cast<uint8_t*>(const_cast<void*>(op.peers[k])) + off;
       cudaError_t e;
-      if (c0 == 0 && c1 == ldc) {
-        e = cudaMemcpyAsync(dst, src, static_cast<size_t>((r1 - r0) * ldc) * 2, cudaMemcpyDefault, cs);
+      if (ldc == N) {
+        e = cudaMemcpyAsync(dst, src, static_cast<size_t>((r1 - r0) * N) * 2, cudaMemcpyDefault, cs);
       } else {
         e = cudaMemcpy2DAsync(dst, static_cast<size_t>(ldc) * 2, src, static_cast<size_t>(ldc) * 2,
-                              static_cast<size_t>(c1 - c0) * 2, static_cast<size_t>(r1 - r0), cudaMemcpyDefault, cs);
+                              static_cast<size_t>(N) * 2, static_cast<size_t>(r1 - r0), cudaMemcpyDefault, cs);
       }
       if (e != cudaSuccess) return fail_cuda(e, "peer copy");
     }
@@ -635,10 +611,7 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
   // copy-engine exchange: the kernel writes only its own C
   p.n_peers = op.copy_exchange ? 0 : op.n_peers;
   p.peer_tma = 0;
-  p.xwalk = 0;
-  p.main_rows = 0;
-  p.n_main = 0;
-  std::memset(p.col_bounds, 0, sizeof(p.col_bounds));
+  p.chunk_rows = 1;
   p.chunk_done = nullptr;
   for (int i = 0; i < kMaxPeers; ++i) {
     p.peer_C[i] = i < op.n_peers ? static_cast<__half*>(const_cast<void*>(op.peers[i])) : nullptr;
@@ -816,10 +789,9 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
   ExchangeEvents* xev = nullptr;
   if (op.copy_exchange) {
     xp = exchange_plan(pl);
-    p.xwalk = 1;
-    p.main_rows = xp.main_rows;
-    p.n_main = xp.n_main;
-    std::memcpy(p.col_bounds, xp.bounds, sizeof(p.col_bounds));
+    p.raster = 0;
+    p.group = xp.chunk_rows;
+    p.chunk_rows = xp.chunk_rows;
     p.chunk_done = op.chunk_counters;
     st = exchange_begin(op, dev, stream, &xev);
     if (st != GEMM_OK) return st;

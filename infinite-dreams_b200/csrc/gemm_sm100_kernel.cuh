@@ -51,7 +51,7 @@ constexpr int kStoreRows = 32;    // rows per epilogue store box (one warp's TME
 constexpr int kStoreCols = 64;    // columns per epilogue store box (128 bytes)
 constexpr int kCounterSlots = 65536;  // split-K tile tickets at the head of the workspace
 constexpr int kMaxPeers = 7;          // peer copies of C (fused all-gather over 8 GPUs)
-constexpr int kMaxMainChunks = 8;     // column chunks of the copy-engine exchange's main region
+constexpr int kMaxChunks = 16;        // row-band chunks of the copy-engine exchange
 
 struct GemmParams {
   int M, N, K;
@@ -97,17 +97,14 @@ struct GemmParams {
   int peer_tma;
   __half* peer_C[kMaxPeers];
   CUtensorMap peer_map[kMaxPeers];
-  // Copy-engine exchange (gemm_launch_gather_copy).  xwalk = 1 walks the
-  // tiles in two regions, each column by column (M fastest): the tile rows
-  // [0, main_rows), then the rest (the tail region, about one wave of
-  // tiles).  Once every box of a tile has landed in C, each epilogue warp
-  // adds 1 to chunk_done[chunk of the tile]: chunk c < n_main is the main
-  // rows' tile columns [col_bounds[c], col_bounds[c + 1]); chunk n_main is
-  // the tail region (whole rows, so one contiguous block of C).  Copy
-  // streams wait on these counts (on the GPU) and then move each chunk to
-  // the peers with the copy engines, while the GEMM goes on.
-  int xwalk, main_rows, n_main;
-  int col_bounds[kMaxMainChunks + 1];
+  // Copy-engine exchange (gemm_launch_gather_copy): the tiles are walked in
+  // groups of chunk_rows tile rows (raster 0, group = chunk_rows), so C is
+  // finished band by band; once every box of a tile has landed in C, each
+  // epilogue warp adds 1 to chunk_done[tile row / chunk_rows].  A band is
+  // whole rows of C, one contiguous block: copy streams wait (on the GPU)
+  // for its count and then move it to the peers with the copy engines while
+  // the GEMM goes on.  chunk_done = null: no counting.
+  int chunk_rows;
   unsigned int* chunk_done;
 };
 
@@ -147,22 +144,8 @@ struct SmemPlan {
   static_assert(kOffB % 1024 == 0 && kOffC % 1024 == 0, "swizzled buffers need 1024-byte alignment");
 };
 
-// Tile index -> (tile row, tile column) in grouped raster order (or the
-// copy-engine exchange's two-region walk).
+// Tile index -> (tile row, tile column) in grouped raster order.
 __device__ __forceinline__ void tile_coords(const GemmParams& p, int t, int& tm, int& tn) {
-  if (p.xwalk) {
-    const int main_tiles = p.main_rows * p.tiles_n;
-    if (t < main_tiles) {
-      tm = t % p.main_rows;
-      tn = t / p.main_rows;
-    } else {
-      const int tail = p.tiles_m - p.main_rows;
-      const int u = t - main_tiles;
-      tm = p.main_rows + u % tail;
-      tn = u / tail;
-    }
-    return;
-  }
   if (p.raster == 0) {
     const int per_group = p.group * p.tiles_n;
     const int g = t / per_group;
@@ -180,14 +163,6 @@ __device__ __forceinline__ void tile_coords(const GemmParams& p, int t, int& tm,
     tn = first + r % gs;
     tm = r / gs;
   }
-}
-
-// Chunk of the copy-engine exchange that tile (tm, tn) belongs to.
-__device__ __forceinline__ int exchange_chunk(const GemmParams& p, int tm, int tn) {
-  if (tm >= p.main_rows) return p.n_main;
-  int c = 0;
-  while (c + 1 < p.n_main && tn >= p.col_bounds[c + 1]) ++c;
-  return c;
 }
 
 // One piece of work: tile (tm, tn), K blocks [kb0, kb1), and which of the
@@ -984,7 +959,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         fence_proxy_async_global();
         __threadfence_system();
         __syncwarp();
-        if (lane == 0) atomicAdd_system(&p.chunk_done[exchange_chunk(p, tm, tn)], 1u);
+        if (lane == 0) atomicAdd_system(&p.chunk_done[tm / p.chunk_rows], 1u);
       }
       if (++acc == Plan::kNumAcc) {
         acc = 0;
@@ -998,7 +973,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       // copies then move whatever is in C, and the error word reports the
       // timeout), so no stream is left waiting on this grid.
       if (p.chunk_done != nullptr && threadIdx.x == 64) {
-        for (int c = 0; c <= p.n_main; ++c) atomicMax(&p.chunk_done[c], 0x3fffffffu);
+        const int chunks = (p.tiles_m + p.chunk_rows - 1) / p.chunk_rows;
+        for (int c = 0; c < chunks; ++c) atomicMax(&p.chunk_done[c], 0x3fffffffu);
       }
     }
     // The staging smem must stay valid until the last TMA stores have read it;

@@ -22,7 +22,7 @@ GEMM_ERR_DEVICE_TIMEOUT = 6
 
 GEMM_MAX_PEERS = 7
 GEMM_IPC_HANDLE_BYTES = 64
-GEMM_GATHER_COUNTERS = 9
+GEMM_GATHER_COUNTERS = 16
 
 GEMM_ACT_NONE = 0
 GEMM_ACT_RELU = 1
