@@ -141,27 +141,6 @@ int gemm_launch_gather(const void* A, const void* B, void* C, int64_t M, int64_t
                        int64_t ldb, int64_t ldc, const void* const* peer_C, int n_peers, int cfg_id,
                        void* workspace, size_t workspace_bytes, void* stream);
 
-/* gemm_launch_gather with the transfer done by the copy engines instead of
- * the kernel's own stores.  The kernel finishes C in bands of whole rows (at
- * most GEMM_GATHER_COUNTERS of them, walked in order), counts finished tiles
- * per band in chunk_counters (device memory of GEMM_GATHER_COUNTERS
- * unsigned ints, caller-owned, not shared by concurrent calls; reset here
- * on `stream`), and copy streams wait on the GPU for a band's count before
- * copying the band -- one contiguous block -- into the peers' C.  The copies
- * overlap the rest of the GEMM and the SMs issue no remote stores.
- * copy_streams[0..n_copy_streams) are created streams other than `stream`
- * (2 * n_peers lets consecutive bands' copies overlap); on return they are
- * joined back into `stream`, so work queued on `stream` afterwards (the
- * closing collective) follows every copy of this rank.  The configuration's
- * raster and group are replaced by the band walk.  Same restrictions as
- * gemm_launch_gather, plus row-major operands and no fused epilogue.
- * Extends the reference, which ran on one GPU. */
-#define GEMM_GATHER_COUNTERS 16
-int gemm_launch_gather_copy(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
-                            int64_t ldb, int64_t ldc, const void* const* peer_C, int n_peers, int cfg_id,
-                            void* workspace, size_t workspace_bytes, void* stream, void* const* copy_streams,
-                            int n_copy_streams, unsigned int* chunk_counters);
-
 /* CUDA IPC of device memory between the processes of one node, for
  * gemm_launch_gather.  gemm_ipc_export writes the GEMM_IPC_HANDLE_BYTES-byte
  * handle of the allocation that holds ptr and ptr's offset inside it;
@@ -172,6 +151,27 @@ int gemm_launch_gather_copy(const void* A, const void* B, void* C, int64_t M, in
 int gemm_ipc_export(const void* ptr, void* handle, int64_t* offset);
 int gemm_ipc_import(const void* handle, int64_t offset, void** ptr);
 int gemm_ipc_close(void* ptr);
+
+/* Stream-ordered helpers for exchanges that must not occupy SMs (the
+ * overlapped all-gather of back-to-back sharded GEMMs, where a persistent
+ * GEMM holds every SM while the previous step's result moves):
+ *   gemm_ipc_copy       bytes from src to dst on `stream` by the copy
+ *                       engines (either side may be a gemm_ipc_import
+ *                       mapping of another GPU's memory);
+ *   gemm_stream_signal  writes `value` to the 32-bit word `flag` (local or
+ *                       mapped peer memory) once earlier work on `stream`
+ *                       is done;
+ *   gemm_stream_wait    holds later work on `stream` until the word at
+ *                       `flag` is >= `value` (compared as a wrapping
+ *                       32-bit difference).
+ * The signal and the wait are executed by the GPU's front end, not by a
+ * kernel.  A wait on a flag that nothing will write holds its stream until
+ * the process exits: a caller that signals from other processes must keep
+ * every process's signals in the same order.  No counterpart in the
+ * reference. */
+int gemm_ipc_copy(void* dst, const void* src, size_t bytes, void* stream);
+int gemm_stream_signal(void* stream, void* flag, uint32_t value);
+int gemm_stream_wait(void* stream, const void* flag, uint32_t value);
 
 /* A reasonable configuration for a shape when no tuned entry exists.
  * No counterpart in the reference (its tuner had no per-shape dispatch). */

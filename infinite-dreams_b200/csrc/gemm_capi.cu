@@ -12,7 +12,6 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
-#include <algorithm>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -230,12 +229,6 @@ struct OpDesc {
   int act = 0;
   const void* const* peers = nullptr;  // fused all-gather targets (gemm_launch_gather)
   int n_peers = 0;
-  // Copy-engine exchange (gemm_launch_gather_copy): the peers are written by
-  // copies on these streams, not by the kernel.
-  bool copy_exchange = false;
-  void* const* copy_streams = nullptr;
-  int n_copy_streams = 0;
-  unsigned int* chunk_counters = nullptr;
   bool epi() const { return alpha != 1.0f || beta != 0.0f || bias != nullptr || act != 0; }
 };
 
@@ -422,131 +415,6 @@ int launch_pack(const void* src, int64_t lds, void* dst, int64_t ldd, int64_t ro
   return e == cudaSuccess ? GEMM_OK : fail_cuda(e, "pack_rows_f16 launch");
 }
 
-// ---------------------------------------------------------------- copy-engine exchange
-
-// Chunks of the copy-engine exchange: bands of whole tile rows, at most
-// kMaxChunks of them, walked in order (raster 0 with group = rows per band,
-// so the tiles of a band are walked column by column and share their B
-// panels in L2).  A band is a contiguous block of C: its copies run at the
-// copy engines' full rate, and the last band -- the part of the exchange
-// that cannot overlap the GEMM -- is at most 1/kMaxChunks of C.
-static_assert(GEMM_GATHER_COUNTERS == kMaxChunks, "one counter per row-band chunk");
-
-struct ExchangePlan {
-  int chunk_rows = 1, n_chunks = 0;
-  uint32_t target[kMaxChunks] = {};   // epilogue-warp signals per chunk
-};
-
-ExchangePlan exchange_plan(const Plan& pl) {
-  ExchangePlan x;
-  x.chunk_rows = (pl.tiles_m + kMaxChunks - 1) / kMaxChunks;
-  x.n_chunks = (pl.tiles_m + x.chunk_rows - 1) / x.chunk_rows;
-  const uint32_t per_tile = static_cast<uint32_t>(kEpiWarps * pl.cg);
-  for (int c = 0; c < x.n_chunks; ++c) {
-    const int rows = std::min(pl.tiles_m, (c + 1) * x.chunk_rows) - c * x.chunk_rows;
-    x.target[c] = per_tile * static_cast<uint32_t>(rows * pl.tiles_n);
-  }
-  return x;
-}
-
-using WaitValueFn = CUresult (*)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
-
-WaitValueFn wait_value_fn() {
-  static WaitValueFn fn = [] {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuStreamWaitValue32", &f, cudaEnableDefault, &q) != cudaSuccess ||
-        q != cudaDriverEntryPointSuccess) {
-      return static_cast<WaitValueFn>(nullptr);
-    }
-    return reinterpret_cast<WaitValueFn>(f);
-  }();
-  return fn;
-}
-
-// Events that order the copy streams against the caller's stream, one set
-// per device and host thread (a record followed by its waits is issued
-// without interleaving).
-constexpr int kMaxCopyStreams = 16;
-struct ExchangeEvents {
-  bool ready = false;
-  cudaEvent_t start = nullptr;
-  cudaEvent_t join[kMaxCopyStreams] = {};
-};
-thread_local ExchangeEvents t_xevents[kMaxDevices];
-
-int exchange_events(int dev, ExchangeEvents** out) {
-  ExchangeEvents& ev = t_xevents[dev];
-  if (!ev.ready) {
-    cudaError_t e = cudaEventCreateWithFlags(&ev.start, cudaEventDisableTiming);
-    for (int i = 0; e == cudaSuccess && i < kMaxCopyStreams; ++i) {
-      e = cudaEventCreateWithFlags(&ev.join[i], cudaEventDisableTiming);
-    }
-    if (e != cudaSuccess) return fail_cuda(e, "cudaEventCreateWithFlags");
-    ev.ready = true;
-  }
-  *out = &ev;
-  return GEMM_OK;
-}
-
-// Before the GEMM: reset the chunk counts and start the copy streams after
-// the reset.
-int exchange_begin(const OpDesc& op, int dev, cudaStream_t stream, ExchangeEvents** evs) {
-  int st = exchange_events(dev, evs);
-  if (st != GEMM_OK) return st;
-  cudaError_t e = cudaMemsetAsync(op.chunk_counters, 0, kMaxChunks * sizeof(unsigned int), stream);
-  if (e != cudaSuccess) return fail_cuda(e, "cudaMemsetAsync(chunk counters)");
-  e = cudaEventRecord((*evs)->start, stream);
-  if (e != cudaSuccess) return fail_cuda(e, "cudaEventRecord");
-  for (int i = 0; i < op.n_copy_streams; ++i) {
-    e = cudaStreamWaitEvent(static_cast<cudaStream_t>(op.copy_streams[i]), (*evs)->start, 0);
-    if (e != cudaSuccess) return fail_cuda(e, "cudaStreamWaitEvent");
-  }
-  return GEMM_OK;
-}
-
-// After the GEMM: on the copy streams, wait (on the GPU) for each band's
-// count, copy the band into every peer's C, then join the copy streams back
-// into the caller's stream.  Bands alternate between two sets of streams
-// (peer k: stream k, then stream n_peers + k, modulo the number of streams),
-// so a band's copies need not queue behind the previous band's.
-int exchange_copies(const OpDesc& op, const Plan& pl, const ExchangePlan& x, const void* C, int64_t M, int64_t N,
-                    int64_t ldc, cudaStream_t stream, ExchangeEvents* evs) {
-  WaitValueFn wait = wait_value_fn();
-  if (!wait) return fail(GEMM_ERR_CUDA, "cuStreamWaitValue32 is not available from the driver");
-  const int64_t bm = static_cast<int64_t>(kBM) * pl.cg * x.chunk_rows;
-  const int S = op.n_copy_streams;
-  for (int c = 0; c < x.n_chunks; ++c) {
-    const int64_t r0 = std::min<int64_t>(M, c * bm), r1 = std::min<int64_t>(M, (c + 1) * bm);
-    const CUdeviceptr flag = reinterpret_cast<CUdeviceptr>(op.chunk_counters + c);
-    for (int k = 0; k < op.n_peers; ++k) {
-      cudaStream_t cs = static_cast<cudaStream_t>(op.copy_streams[(k + (c % 2) * op.n_peers) % S]);
-      CUresult r = wait(reinterpret_cast<CUstream>(cs), flag, x.target[c], CU_STREAM_WAIT_VALUE_GEQ);
-      if (r != CUDA_SUCCESS) {
-        return fail(GEMM_ERR_CUDA, "cuStreamWaitValue32 failed with CUresult " + std::to_string(static_cast<int>(r)));
-      }
-      if (r1 <= r0) continue;
-      const size_t off = static_cast<size_t>(r0 * ldc) * 2;
-      const uint8_t* src = static_cast<const uint8_t*>(C) + off;
-      uint8_t* dst = static_cast<uint8_t*>(const_cast<void*>(op.peers[k])) + off;
-      cudaError_t e;
-      if (ldc == N) {
-        e = cudaMemcpyAsync(dst, src, static_cast<size_t>((r1 - r0) * N) * 2, cudaMemcpyDefault, cs);
-      } else {
-        e = cudaMemcpy2DAsync(dst, static_cast<size_t>(ldc) * 2, src, static_cast<size_t>(ldc) * 2,
-                              static_cast<size_t>(N) * 2, static_cast<size_t>(r1 - r0), cudaMemcpyDefault, cs);
-      }
-      if (e != cudaSuccess) return fail_cuda(e, "peer copy");
-    }
-  }
-  for (int i = 0; i < S; ++i) {
-    cudaError_t e = cudaEventRecord(evs->join[i], static_cast<cudaStream_t>(op.copy_streams[i]));
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(stream, evs->join[i], 0);
-    if (e != cudaSuccess) return fail_cuda(e, "joining the copy streams");
-  }
-  return GEMM_OK;
-}
-
 int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
                 int64_t ldc, const OpDesc& op, int cfg_id, void* ws, size_t ws_bytes, void* stream_v) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
@@ -608,11 +476,8 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
   p.D = op.beta != 0.0f ? static_cast<const __half*>(op.D) : nullptr;
   p.ldd = op.beta != 0.0f ? op.ldd : 0;
   p.bias = static_cast<const __half*>(op.bias);
-  // copy-engine exchange: the kernel writes only its own C
-  p.n_peers = op.copy_exchange ? 0 : op.n_peers;
+  p.n_peers = op.n_peers;
   p.peer_tma = 0;
-  p.chunk_rows = 1;
-  p.chunk_done = nullptr;
   for (int i = 0; i < kMaxPeers; ++i) {
     p.peer_C[i] = i < op.n_peers ? static_cast<__half*>(const_cast<void*>(op.peers[i])) : nullptr;
   }
@@ -620,25 +485,6 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
   if (op.n_peers > 0 && (pl.skinny || pl.max_parts > 1 || K == 0)) {
     return fail(GEMM_ERR_UNSUPPORTED, "the fused all-gather needs K > 0 and a configuration without split-K / "
                                       "stream-K and with tile_m >= 128");
-  }
-  if (op.copy_exchange) {
-    if (pl.skinny || pl.max_parts > 1 || K == 0 || op.epi() || op.trans_a || op.trans_b) {
-      return fail(GEMM_ERR_UNSUPPORTED, "the copy-engine exchange needs K > 0, row-major operands, no fused "
-                                        "epilogue and a configuration without split-K / stream-K with tile_m >= 128");
-    }
-    if (!op.copy_streams || op.n_copy_streams < 1 || op.n_copy_streams > kMaxCopyStreams) {
-      return fail(GEMM_ERR_INVALID_ARG, "the copy-engine exchange needs 1 to " + std::to_string(kMaxCopyStreams) +
-                                            " copy streams");
-    }
-    for (int i = 0; i < op.n_copy_streams; ++i) {
-      if (!op.copy_streams[i] || op.copy_streams[i] == stream_v) {
-        return fail(GEMM_ERR_INVALID_ARG, "copy streams must be created streams, other than the launch stream");
-      }
-    }
-    if (!op.chunk_counters || reinterpret_cast<uintptr_t>(op.chunk_counters) % 4u) {
-      return fail(GEMM_ERR_INVALID_ARG, "chunk_counters must be a 4-byte aligned device array of "
-                                        "GEMM_GATHER_COUNTERS unsigned ints");
-    }
   }
   if (K == 0) {
     // Empty reduction: C = 0 (the reference kernel's loop body never runs),
@@ -785,23 +631,10 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
   p.partials = pl.max_parts > 1 ? reinterpret_cast<float*>(wsb + pl.off_partials) : nullptr;
   p.counters = pl.max_parts > 1 ? reinterpret_cast<unsigned int*>(wsb) : nullptr;
 
-  ExchangePlan xp;
-  ExchangeEvents* xev = nullptr;
-  if (op.copy_exchange) {
-    xp = exchange_plan(pl);
-    p.raster = 0;
-    p.group = xp.chunk_rows;
-    p.chunk_rows = xp.chunk_rows;
-    p.chunk_done = op.chunk_counters;
-    st = exchange_begin(op, dev, stream, &xev);
-    if (st != GEMM_OK) return st;
-  }
-
   // persistent grid: one CTA (or CTA pair) per SM (pair), at most one per work unit
   const int grid = pl.workers * pl.cg;
   e = var->fn(tmA, tmB, tmC, p, grid, stream);
   if (e != cudaSuccess) return fail_cuda(e, "gemm kernel launch");
-  if (op.copy_exchange) return exchange_copies(op, pl, xp, C, M, N, ldc, stream, xev);
   return GEMM_OK;
 }
 
@@ -910,21 +743,6 @@ int gemm_launch_gather(const void* A, const void* B, void* C, int64_t M, int64_t
   return launch_impl(A, B, C, M, N, K, lda, ldb, ldc, op, cfg_id, workspace, workspace_bytes, stream);
 }
 
-int gemm_launch_gather_copy(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
-                            int64_t ldb, int64_t ldc, const void* const* peer_C, int n_peers, int cfg_id,
-                            void* workspace, size_t workspace_bytes, void* stream, void* const* copy_streams,
-                            int n_copy_streams, unsigned int* chunk_counters) {
-  t_last_error.clear();
-  OpDesc op;
-  op.peers = peer_C;
-  op.n_peers = n_peers;
-  op.copy_exchange = true;
-  op.copy_streams = copy_streams;
-  op.n_copy_streams = n_copy_streams;
-  op.chunk_counters = chunk_counters;
-  return launch_impl(A, B, C, M, N, K, lda, ldb, ldc, op, cfg_id, workspace, workspace_bytes, stream);
-}
-
 int gemm_ipc_export(const void* ptr, void* handle, int64_t* offset) {
   t_last_error.clear();
   if (!ptr || !handle || !offset) return fail(GEMM_ERR_INVALID_ARG, "ptr, handle and offset must be non-null");
@@ -979,6 +797,50 @@ int gemm_ipc_close(void* ptr) {
   }
   cudaError_t e = cudaIpcCloseMemHandle(base);
   return e == cudaSuccess ? GEMM_OK : fail_cuda(e, "cudaIpcCloseMemHandle");
+}
+
+namespace {
+
+using StreamValueFn = CUresult (*)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
+
+StreamValueFn stream_value_fn(const char* name) {
+  void* f = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &f, cudaEnableDefault, &q) != cudaSuccess || q != cudaDriverEntryPointSuccess) {
+    return nullptr;
+  }
+  return reinterpret_cast<StreamValueFn>(f);
+}
+
+}  // namespace
+
+int gemm_ipc_copy(void* dst, const void* src, size_t bytes, void* stream) {
+  t_last_error.clear();
+  if (bytes == 0) return GEMM_OK;
+  if (!dst || !src) return fail(GEMM_ERR_INVALID_ARG, "dst and src must be non-null");
+  cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? GEMM_OK : fail_cuda(e, "cudaMemcpyAsync");
+}
+
+int gemm_stream_signal(void* stream, void* flag, uint32_t value) {
+  t_last_error.clear();
+  static StreamValueFn fn = stream_value_fn("cuStreamWriteValue32");
+  if (!fn) return fail(GEMM_ERR_CUDA, "cuStreamWriteValue32 is not available from the driver");
+  if (!flag || reinterpret_cast<uintptr_t>(flag) % 4u) return fail(GEMM_ERR_INVALID_ARG, "flag must be 4-byte aligned");
+  CUresult r = fn(static_cast<CUstream>(stream), reinterpret_cast<CUdeviceptr>(flag), value,
+                  CU_STREAM_WRITE_VALUE_DEFAULT);
+  return r == CUDA_SUCCESS ? GEMM_OK
+                           : fail(GEMM_ERR_CUDA, "cuStreamWriteValue32 failed with CUresult " + std::to_string(r));
+}
+
+int gemm_stream_wait(void* stream, const void* flag, uint32_t value) {
+  t_last_error.clear();
+  static StreamValueFn fn = stream_value_fn("cuStreamWaitValue32");
+  if (!fn) return fail(GEMM_ERR_CUDA, "cuStreamWaitValue32 is not available from the driver");
+  if (!flag || reinterpret_cast<uintptr_t>(flag) % 4u) return fail(GEMM_ERR_INVALID_ARG, "flag must be 4-byte aligned");
+  CUresult r = fn(static_cast<CUstream>(stream), reinterpret_cast<CUdeviceptr>(flag), value, CU_STREAM_WAIT_VALUE_GEQ);
+  return r == CUDA_SUCCESS ? GEMM_OK
+                           : fail(GEMM_ERR_CUDA, "cuStreamWaitValue32 failed with CUresult " + std::to_string(r));
 }
 
 int gemm_launch_knobs(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,

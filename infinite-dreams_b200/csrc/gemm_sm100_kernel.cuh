@@ -51,7 +51,6 @@ constexpr int kStoreRows = 32;    // rows per epilogue store box (one warp's TME
 constexpr int kStoreCols = 64;    // columns per epilogue store box (128 bytes)
 constexpr int kCounterSlots = 65536;  // split-K tile tickets at the head of the workspace
 constexpr int kMaxPeers = 7;          // peer copies of C (fused all-gather over 8 GPUs)
-constexpr int kMaxChunks = 16;        // row-band chunks of the copy-engine exchange
 
 struct GemmParams {
   int M, N, K;
@@ -97,15 +96,6 @@ struct GemmParams {
   int peer_tma;
   __half* peer_C[kMaxPeers];
   CUtensorMap peer_map[kMaxPeers];
-  // Copy-engine exchange (gemm_launch_gather_copy): the tiles are walked in
-  // groups of chunk_rows tile rows (raster 0, group = chunk_rows), so C is
-  // finished band by band; once every box of a tile has landed in C, each
-  // epilogue warp adds 1 to chunk_done[tile row / chunk_rows].  A band is
-  // whole rows of C, one contiguous block: copy streams wait (on the GPU)
-  // for its count and then move it to the peers with the copy engines while
-  // the GEMM goes on.  chunk_done = null: no counting.
-  int chunk_rows;
-  unsigned int* chunk_done;
 };
 
 template <int BN, int STAGES, int CG>
@@ -952,15 +942,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) release_acc(kHalvesEpi ? 1 : acc);
-      if (p.chunk_done != nullptr) {
-        // Every box of this warp's part of the tile is in C (TMA stores
-        // complete, plain stores fenced) before the chunk's count moves.
-        if (lane == 0 && p.c_tma) bulk_wait_group<0>();
-        fence_proxy_async_global();
-        __threadfence_system();
-        __syncwarp();
-        if (lane == 0) atomicAdd_system(&p.chunk_done[tm / p.chunk_rows], 1u);
-      }
       if (++acc == Plan::kNumAcc) {
         acc = 0;
         acc_phase ^= 1u;
@@ -969,13 +950,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     if (!ok) {
       *abort_flag = 1;
       atomicOr(p.err, kDevErrTimeoutEpilogue);
-      // The copy streams wait on the chunk counts: release them all (the
-      // copies then move whatever is in C, and the error word reports the
-      // timeout), so no stream is left waiting on this grid.
-      if (p.chunk_done != nullptr && threadIdx.x == 64) {
-        const int chunks = (p.tiles_m + p.chunk_rows - 1) / p.chunk_rows;
-        for (int c = 0; c < chunks; ++c) atomicMax(&p.chunk_done[c], 0x3fffffffu);
-      }
     }
     // The staging smem must stay valid until the last TMA stores have read it;
     // their global writes complete with the grid.

@@ -210,12 +210,6 @@ __device__ __forceinline__ void bulk_wait_group() {
   asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// Orders this thread's async-proxy accesses of global memory (completed
-// TMA stores) with its later generic-proxy accesses.
-__device__ __forceinline__ void fence_proxy_async_global() {
-  asm volatile("fence.proxy.async.global;" ::: "memory");
-}
-
 // Make generic-proxy writes to shared memory visible to the async proxy
 // (TMA store / tcgen05.mma operand reads).
 __device__ __forceinline__ void fence_proxy_async_smem() {

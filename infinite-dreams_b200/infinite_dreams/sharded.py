@@ -21,14 +21,13 @@ the launch on the same stream marks the point where every rank's grid, and
 with it every write into this rank's C, has completed.  No kernel reads
 another GPU's memory; peers are only written to.
 
-``exchange="copy"`` uses the same buffers, but the bytes cross NVLink by the
-copy engines (``gemm_launch_gather_copy``): the kernel finishes C in chunks
-and counts finished tiles per chunk, and per-peer copy streams wait on the
-GPU for each chunk's count before copying it into the peers' C.  Remote
-stores from the SMs share their path to memory with the GEMM's own operand
-loads; when the links are busy the loads queue behind them.  The copy
-engines take that traffic off the SMs, so the GEMM runs at its own speed
-while the exchange proceeds.
+``OverlappedGather`` runs back-to-back GEMMs of one shape and overlaps each
+step's all-gather with the next step's GEMM: once a rank's GEMM has
+finished, copy streams move its row block into every other rank's C with the
+copy engines (one contiguous block per peer over NVLink), while the next
+GEMM computes.  Remote stores issued by the SMs share the SMs' path to
+memory with the GEMM's own operand loads, and when the links are busy the
+loads queue behind them; the copy engines keep that traffic off the SMs.
 """
 from __future__ import annotations
 
@@ -72,18 +71,17 @@ def sharded_gemm(A_local: torch.Tensor, B: torch.Tensor, M_total: Optional[int] 
     kernel-bank GEMM.  ``chunks`` > 1 overlaps the all-gather with the
     compute (equal row blocks only; other cases fall back to one exchange).
     ``exchange="fused"`` (gather=True, CUDA, equal row blocks) writes every
-    tile to all ranks from inside the GEMM; ``exchange="copy"`` moves the
-    finished chunks of C with the copy engines while the GEMM runs.  In both
-    the returned full C is a buffer owned by this module: it stays intact
-    until the second such call of that shape after this one, provided
-    whatever reads it is issued on the calling stream before the next call.
+    tile to all ranks from inside the GEMM; the returned full C is a buffer
+    owned by this module: it stays intact until the second fused call of
+    that shape after this one, provided whatever reads it is issued on the
+    calling stream before the next fused call.
     """
-    if exchange not in ("nccl", "fused", "copy"):
-        raise ValueError("exchange must be 'nccl', 'fused' or 'copy'")
-    if exchange in ("fused", "copy") and gather and dist.is_initialized() and dist.get_world_size(group) > 1:
+    if exchange not in ("nccl", "fused"):
+        raise ValueError("exchange must be 'nccl' or 'fused'")
+    if exchange == "fused" and gather and dist.is_initialized() and dist.get_world_size(group) > 1:
         if out is not None or compute is not None:
-            raise ValueError(f"exchange='{exchange}' owns its output buffer and runs the kernel bank itself")
-        return _fused_gather(A_local, B, M_total, group, copy_engines=(exchange == "copy"))
+            raise ValueError("exchange='fused' owns its output buffer and runs the kernel bank itself")
+        return _fused_gather(A_local, B, M_total, group)
     compute = compute or _default_compute
     if gather and chunks > 1 and dist.is_initialized() and dist.get_world_size(group) > 1:
         full = _pipelined_gather(A_local, B, M_total, group, out, compute, chunks)
@@ -242,26 +240,7 @@ def _gather_cfg(rows: int, N: int, K: int) -> int:
     return _capi.cfg_find(fallback)
 
 
-_copy_res: Dict[int, Tuple[List[torch.cuda.Stream], torch.Tensor]] = {}
-
-
-def _copy_resources(device: torch.device, n_peers: int) -> Tuple[List[torch.cuda.Stream], torch.Tensor]:
-    """Per device: 2 * n_peers copy streams (a peer's last chunk gets a
-    stream of its own) and the chunk counters of the copy-engine exchange."""
-    from . import _capi
-
-    with _ipc_lock:
-        res = _copy_res.get(device.index)
-        if res is None or len(res[0]) < 2 * n_peers:
-            streams = [torch.cuda.Stream(device) for _ in range(2 * n_peers)]
-            counters = torch.zeros(_capi.GEMM_GATHER_COUNTERS, dtype=torch.int32, device=device)
-            res = (streams, counters)
-            _copy_res[device.index] = res
-    return res
-
-
-def _fused_gather(A_local: torch.Tensor, B: torch.Tensor, M_total: Optional[int], group,
-                  copy_engines: bool = False) -> torch.Tensor:
+def _fused_gather(A_local: torch.Tensor, B: torch.Tensor, M_total: Optional[int], group) -> torch.Tensor:
     from . import _capi, infinite_dreams_ext as ext
 
     if not (A_local.is_cuda and B.is_cuda):
@@ -284,22 +263,178 @@ def _fused_gather(A_local: torch.Tensor, B: torch.Tensor, M_total: Optional[int]
         stream = torch.cuda.current_stream(device)
         need = _capi.lib.gemm_workspace_bytes(A_local.data_ptr(), B.data_ptr(), rows, N, K, K, N, cid)
         ws_ptr, ws_len = ext._workspace(device, stream, need) if need else (0, 0)
-        if copy_engines:
-            streams, counters = _copy_resources(device, len(targets))
-            carr = (ctypes.c_void_p * len(streams))(*[s.cuda_stream for s in streams])
-            _capi.check(_capi.lib.gemm_launch_gather_copy(
-                A_local.data_ptr(), B.data_ptr(), mine.data_ptr(), rows, N, K, K, N, N, arr, len(targets), cid,
-                ws_ptr or None, ws_len, stream.cuda_stream or None, carr, len(streams), counters.data_ptr()),
-                "gemm_launch_gather_copy")
-        else:
-            _capi.check(_capi.lib.gemm_launch_gather(A_local.data_ptr(), B.data_ptr(), mine.data_ptr(), rows, N, K, K,
-                                                     N, N, arr, len(targets), cid, ws_ptr or None, ws_len,
-                                                     stream.cuda_stream or None), "gemm_launch_gather")
+        _capi.check(_capi.lib.gemm_launch_gather(A_local.data_ptr(), B.data_ptr(), mine.data_ptr(), rows, N, K, K, N,
+                                                 N, arr, len(targets), cid, ws_ptr or None, ws_len,
+                                                 stream.cuda_stream or None), "gemm_launch_gather")
         # Ordered after this rank's grid on its stream: completes once every
         # rank's grid (and so every write into this rank's C) has finished.
         done = torch.zeros(1, dtype=torch.float32, device=device)
         dist.all_reduce(done, group=group)
     return full
+
+
+class GatherResult:
+    """The whole C of one OverlappedGather step on this rank."""
+
+    def __init__(self, full: torch.Tensor, done: torch.cuda.Event):
+        self.full = full
+        self._done = done
+
+    def wait(self, stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+        """Makes `stream` (default: the current stream) wait until every
+        rank's rows of this step are in ``full``; returns ``full``."""
+        (stream or torch.cuda.current_stream(self.full.device)).wait_event(self._done)
+        return self.full
+
+
+class OverlappedGather:
+    """Back-to-back sharded GEMMs of one shape, each step's all-gather of C
+    overlapping the next step's GEMM.
+
+    Every rank holds two full-size C buffers, used by alternate steps, which
+    the other ranks map (CUDA IPC), and a small array of step flags, which
+    they map too.  ``step(A_local, B)`` launches this rank's GEMM into its
+    rows of the step's buffer on the calling stream; then, on side streams
+    and without any kernel:
+
+    1. once the GEMM is done, this rank's flag in every peer's array is set
+       to 2i+1 and the side stream waits until every peer has set its flag
+       here to 2i+1 -- every rank's GEMM of step i is done, so every rank
+       has issued its reads of the result of step i-2, which lives in the
+       same buffer;
+    2. the copy engines copy this rank's rows (one contiguous block) into
+       every peer's buffer, one copy stream per peer;
+    3. the flags go to 2i+2 the same way: every rank's copies of step i are
+       done, so this rank's buffer holds the whole C of step i.
+
+    The GEMM of step i+1 runs while the copies of step i proceed.  The flag
+    writes and waits are stream memory operations, executed by the GPU's
+    front end, so they need no SM while a persistent GEMM holds all of them
+    (a collective would, and would start only after that GEMM).  Every rank
+    must call ``step`` the same number of times.
+
+    ``step`` returns a ``GatherResult``: ``wait()`` orders the calling
+    stream after the step's exchange.  The buffer stays intact until the
+    step after next is called, so reads of it must be issued (after
+    ``wait()``) before then.  ``close()`` (collective) unmaps the peers'
+    memory.
+    """
+
+    def __init__(self, rows: int, N: int, K: int, device: torch.device, group=None, cfg_id: Optional[int] = None):
+        from . import _capi, dispatch
+
+        self.group = group
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        if self.world - 1 > _capi.GEMM_MAX_PEERS:
+            raise ValueError(f"OverlappedGather supports at most {_capi.GEMM_MAX_PEERS + 1} ranks")
+        if not _equal_rows(rows, device, group):
+            raise ValueError("OverlappedGather needs equal row blocks on every rank")
+        self.rows, self.N, self.K, self.device = rows, N, K, device
+        self.cfg_id = dispatch.lookup(rows, N, K) if cfg_id is None else cfg_id
+        # Two buffers of the whole C; the first one carries the step flags
+        # after its C: flags[r] is the last stage that rank r reported here.
+        c_bytes = rows * self.world * N * 2
+        self._raw = [torch.zeros(c_bytes + (4096 if j == 0 else 0), dtype=torch.uint8, device=device)
+                     for j in range(2)]
+        self.flags = self._raw[0][c_bytes:c_bytes + 4 * 64].view(torch.int32)
+        self.bufs = []
+        for raw in self._raw:
+            full = raw[:c_bytes].view(torch.float16).view(rows * self.world, N)
+            self.bufs.append((full, self._map_peers(raw)))
+        self.peer_flags = [None if p is None else p + c_bytes for p in self.bufs[0][1]]
+        self.streams = [torch.cuda.Stream(device) for _ in range(max(1, self.world - 1))]
+        self.copied: List[Optional[torch.cuda.Event]] = [None, None]
+        self.i = 0
+
+    def _map_peers(self, raw: torch.Tensor) -> List[Optional[int]]:
+        """Every other rank's counterpart of `raw`, mapped into this process."""
+        from . import _capi
+
+        handle = (ctypes.c_char * _capi.GEMM_IPC_HANDLE_BYTES)()
+        offset = ctypes.c_int64(0)
+        _capi.check(_capi.lib.gemm_ipc_export(raw.data_ptr(), handle, ctypes.byref(offset)), "gemm_ipc_export")
+        shared: List[Optional[Tuple[bytes, int]]] = [None] * self.world
+        torch.cuda.synchronize(self.device)   # the zeroed flags are in memory before any peer maps them
+        dist.all_gather_object(shared, (bytes(handle), offset.value), group=self.group)
+        out: List[Optional[int]] = []
+        for r, (h, off) in enumerate(shared):
+            if r == self.rank:
+                out.append(None)
+                continue
+            ptr = ctypes.c_void_p()
+            _capi.check(_capi.lib.gemm_ipc_import(h, off, ctypes.byref(ptr)), "gemm_ipc_import")
+            out.append(int(ptr.value))
+        return out
+
+    def _barrier(self, s: torch.cuda.Stream, value: int) -> None:
+        """Tells every peer (on stream s) that this rank reached `value`, then
+        holds s until every peer has reached it too."""
+        from . import _capi
+
+        lib = _capi.lib
+        for r, base in enumerate(self.peer_flags):
+            if base is not None:
+                _capi.check(lib.gemm_stream_signal(s.cuda_stream, base + 4 * self.rank, value), "gemm_stream_signal")
+        for r in range(self.world):
+            if r != self.rank:
+                _capi.check(lib.gemm_stream_wait(s.cuda_stream, self.flags.data_ptr() + 4 * r, value),
+                            "gemm_stream_wait")
+
+    def step(self, A_local: torch.Tensor, B: torch.Tensor) -> GatherResult:
+        from . import _capi, infinite_dreams_ext as ext
+
+        if tuple(A_local.shape) != (self.rows, self.K) or tuple(B.shape) != (self.K, self.N):
+            raise ValueError("OverlappedGather.step: A_local must be rows x K and B K x N, as constructed")
+        i, b = self.i, self.i % 2
+        self.i += 1
+        full, peers = self.bufs[b]
+        mine = full[self.rank * self.rows:(self.rank + 1) * self.rows]
+        stream = torch.cuda.current_stream(self.device)
+        if self.copied[b] is not None:
+            stream.wait_event(self.copied[b])       # this rank's copies of step i-2 read these rows
+        ext.gemm_forward_cfg(A_local, B, self.cfg_id, out=mine)
+        computed = torch.cuda.Event()
+        computed.record(stream)
+        s0 = self.streams[0]
+        s0.wait_event(computed)
+        self._barrier(s0, 2 * i + 1)
+        started = torch.cuda.Event()
+        started.record(s0)
+        offset = self.rank * self.rows * self.N * 2
+        nbytes = self.rows * self.N * 2
+        targets = [p for p in peers if p is not None]
+        for k, base in enumerate(targets):
+            s = self.streams[k]
+            if k:
+                s.wait_event(started)
+            _capi.check(_capi.lib.gemm_ipc_copy(base + offset, mine.data_ptr(), nbytes, s.cuda_stream),
+                        "gemm_ipc_copy")
+        for s in self.streams[1:len(targets)]:
+            ev = torch.cuda.Event()
+            ev.record(s)
+            s0.wait_event(ev)
+        copied = torch.cuda.Event()
+        copied.record(s0)
+        self.copied[b] = copied
+        self._barrier(s0, 2 * i + 2)
+        done = torch.cuda.Event()
+        done.record(s0)
+        return GatherResult(full, done)
+
+    def close(self) -> None:
+        """Collective: waits for outstanding work, unmaps the peers' memory,
+        and frees this rank's buffers once no rank has them mapped."""
+        from . import _capi
+
+        torch.cuda.synchronize(self.device)
+        for _, peers in self.bufs:
+            for ptr in peers:
+                if ptr is not None:
+                    _capi.check(_capi.lib.gemm_ipc_close(ptr), "gemm_ipc_close")
+        self.bufs, self.peer_flags = [], []
+        dist.barrier(group=self.group)
+        self._raw = []
+        self.flags = None
 
 
 def release_peer_buffers(group=None) -> None:

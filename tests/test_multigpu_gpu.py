@@ -49,11 +49,23 @@ def _worker(rank, world, port, M, N, K, q):
         if M % world == 0:
             # tiles written into every rank's C over NVLink by the GEMM itself; three calls, so that
             # one of the two alternating buffers is reused after being overwritten with NaN
-            for exchange in ("fused", "fused", "fused", "copy", "copy", "copy"):
-                F = sharded_gemm(A_local, Bd, M_total=M, gather=True, exchange=exchange)
+            for _ in range(3):
+                F = sharded_gemm(A_local, Bd, M_total=M, gather=True, exchange="fused")
                 torch.cuda.synchronize()
                 fused.append(F.cpu().numpy().view(np.uint16).copy())
                 F.fill_(float("nan"))   # the next call must rewrite every element
+            # back-to-back steps whose all-gathers overlap the next step's GEMM, alternating two inputs:
+            # each result is read right after its wait (before the step after next)
+            from infinite_dreams.sharded import OverlappedGather
+            A2, _ = make_inputs(M, N, K, seed=6)
+            A2_local = A2[r0:r1].contiguous().to(dev)
+            og = OverlappedGather(r1 - r0, N, K, dev)
+            for s in range(4):
+                res = og.step(A_local if s % 2 == 0 else A2_local, Bd)
+                full = res.wait()
+                torch.cuda.synchronize()
+                fused.append(("overlapped", s % 2, full.cpu().numpy().view(np.uint16).copy()))
+            og.close()
         else:
             try:
                 sharded_gemm(A_local, Bd, M_total=M, gather=True, exchange="fused")
@@ -85,18 +97,21 @@ def test_sharded_gemm_nccl_allgather(cuda_device, M):
         p.join(timeout=120)
         assert p.exitcode == 0
     A, B = make_inputs(M, N, K, seed=5)
-    ref = oracle_gemm(A, B).astype(np.float32)
-    tol = 1e-2 * np.sqrt(K / 1024) * np.abs(ref).max() + 1e-3
+    A2, _ = make_inputs(M, N, K, seed=6)
+    refs = [oracle_gemm(A, B).astype(np.float32), oracle_gemm(A2, B).astype(np.float32)]
+    ref = refs[0]
+    tol = max(1e-2 * np.sqrt(K / 1024) * np.abs(r).max() + 1e-3 for r in refs)
     for rank, c, fused in results:
         got = c.view(np.float16).astype(np.float32)
         assert got.shape == ref.shape
         assert np.abs(got - ref).max() <= tol, rank
         for f in fused:
             assert not isinstance(f, str), f
+            which, f = (f[1], f[2]) if isinstance(f, tuple) else (0, f)
             g = f.view(np.float16).astype(np.float32)
             assert g.shape == ref.shape and np.isfinite(g).all(), rank
-            assert np.abs(g - ref).max() <= tol, ("fused", rank)
-        assert len(fused) == (6 if M % world == 0 else 0)
+            assert np.abs(g - refs[which]).max() <= tol, ("fused / overlapped", rank, which)
+        assert len(fused) == (7 if M % world == 0 else 0)
 
 
 def _worker_large(rank, world, port, S, q):
@@ -136,7 +151,10 @@ def _worker_large(rank, world, port, S, q):
         C = sharded_gemm(A_local, Bd, M_total=S, gather=True)
         F = sharded_gemm(A_local, Bd, M_total=S, gather=True, exchange="fused")
         torch.cuda.synchronize()
-        G = sharded_gemm(A_local, Bd, M_total=S, gather=True, exchange="copy")
+        from infinite_dreams.sharded import OverlappedGather
+        og = OverlappedGather(rows, S, S, dev)
+        og.step(A_local, Bd)
+        G = og.step(A_local, Bd).wait()
         torch.cuda.synchronize()
         # first, last and two inner rows of every rank's block
         picks = [r * rows + i for r in range(world) for i in (0, rows // 3, (2 * rows) // 3, rows - 1)]
@@ -153,6 +171,7 @@ def _worker_large(rank, world, port, S, q):
         err_g = float(np.abs(got_g - ref).max()) if np.isfinite(got_g).all() else float("inf")
         q.put((rank, err_c, max(err_f, err_g), tol))
         del F, G
+        og.close()
         release_peer_buffers()
         dist.barrier(device_ids=[rank])
     finally:
@@ -161,7 +180,7 @@ def _worker_large(rank, world, port, S, q):
 
 def test_sharded_16384_cubed_sampled_rows(cuda_device):
     """The bench workload (16384^3, A row-sharded over every GPU, B replicated): the NCCL all-gather, the
-    fused exchange and the copy-engine exchange all give every rank a C whose sampled rows match the oracle."""
+    fused exchange and the overlapped steps all give every rank a C whose sampled rows match the oracle."""
     world = min(torch.cuda.device_count(), 8)
     if world < 2:
         pytest.skip("needs 2 or more GPUs")
@@ -177,4 +196,4 @@ def test_sharded_16384_cubed_sampled_rows(cuda_device):
         assert p.exitcode == 0
     for rank, err_c, err_f, tol in results:
         assert err_c <= tol, ("nccl all-gather", rank, err_c, tol)
-        assert err_f <= tol, ("fused and copy-engine exchanges", rank, err_f, tol)
+        assert err_f <= tol, ("fused exchange and overlapped steps", rank, err_f, tol)
