@@ -205,6 +205,7 @@ struct Plan {
   bool streamk = false;
   int workers = 0;    // persistent CTAs (CTA pairs for cg = 2)
   int dp_tiles = 0;   // stream-K: tiles walked data-parallel first
+  int sk_workers = 0;  // stream-K: workers sharing the stream-K region
   int64_t sk_iters = 0;  // stream-K: iterations of the stream-K region
   int max_parts = 1;  // partial slots per tile
   bool pack_a = false, pack_b = false;
@@ -288,18 +289,29 @@ int make_plan(const void* A, const void* B, int64_t M, int64_t N, int64_t K, int
   pl->workers = static_cast<int>(units < slots ? units : slots);
   pl->max_parts = pl->split_k;
   if (pl->streamk) {
-    // Hybrid stream-K: all full waves but the last run data-parallel; the
-    // remaining 1-2 waves' worth of tiles are split evenly by iterations.
+    // Hybrid stream-K.  A last wave at most half full: every full wave runs
+    // data-parallel and the last wave's R tiles are split over 2R workers,
+    // each tile in two K halves (2 partial slots, one fix-up).  Otherwise
+    // all full waves but the last run data-parallel and the remaining 1-2
+    // waves' worth of tiles are split evenly by iterations over all workers.
     const int64_t T_all = static_cast<int64_t>(pl->num_tiles) * pl->kb_total;
     pl->workers = static_cast<int>(T_all < slots ? T_all : slots);
     const int64_t full_waves = pl->num_tiles / pl->workers;
-    pl->dp_tiles = static_cast<int>(full_waves > 1 ? (full_waves - 1) * pl->workers : 0);
+    const int64_t rem = pl->num_tiles - full_waves * pl->workers;
+    pl->sk_workers = pl->workers;
+    if (full_waves >= 1 && rem > 0 && 2 * rem <= pl->workers && pl->kb_total >= 2) {
+      pl->dp_tiles = static_cast<int>(full_waves * pl->workers);
+      pl->sk_workers = static_cast<int>(2 * rem);
+    } else {
+      pl->dp_tiles = static_cast<int>(full_waves > 1 ? (full_waves - 1) * pl->workers : 0);
+    }
     const int64_t T = static_cast<int64_t>(pl->num_tiles - pl->dp_tiles) * pl->kb_total;
     pl->sk_iters = T;
     int64_t mp = 1;
     for (int64_t tile = pl->dp_tiles; tile < pl->num_tiles; ++tile) {
       const int64_t t0 = (tile - pl->dp_tiles) * pl->kb_total;
-      const int64_t parts = sk_owner(t0 + pl->kb_total - 1, T, pl->workers) - sk_owner(t0, T, pl->workers) + 1;
+      const int64_t parts =
+          sk_owner(t0 + pl->kb_total - 1, T, pl->sk_workers) - sk_owner(t0, T, pl->sk_workers) + 1;
       if (parts > mp) mp = parts;
     }
     pl->max_parts = static_cast<int>(mp);
@@ -624,6 +636,7 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
   p.streamk = pl.streamk ? 1 : 0;
   p.max_parts = pl.max_parts;
   p.dp_tiles = pl.dp_tiles;
+  p.sk_workers = pl.streamk ? pl.sk_workers : pl.workers;
   p.total_iters = pl.streamk ? pl.sk_iters : static_cast<long long>(pl.num_tiles) * pl.kb_total;
   p.raster = pl.raster;
   p.group = pl.group;

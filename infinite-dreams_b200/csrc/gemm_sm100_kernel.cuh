@@ -62,6 +62,7 @@ struct GemmParams {
   int dp_tiles;   // stream-K: whole tiles walked data-parallel before the stream-K region
   int max_parts;  // partial slots per tile in the workspace (split_k, or the most stream-K pieces of any tile)
   long long total_iters;  // stream-K: (num_tiles - dp_tiles) * kb_total iterations of the stream-K region
+  int sk_workers; // stream-K: workers [0, sk_workers) share the stream-K region (<= the grid's workers)
   int raster;     // 0: groups of `group` tile-rows, M fastest; 1: groups of tile-columns, N fastest
   int group;      // >= 1
   int c_tma;      // 1: TMA-store epilogue; 0: coalesced st.global epilogue (any pitch)
@@ -170,13 +171,15 @@ struct Unit {
 //    walks K from the end (serpentine order): consecutive waves share operand
 //    blocks, and the K slices a wave touched last are the ones still in L2.
 //  * stream-K (hybrid): the first dp_tiles tiles are walked data-parallel as
-//    above, whole tiles in waves; the last one to two waves' worth of tiles
-//    form the stream-K region, whose T = (num_tiles - dp_tiles) * kb_total
-//    (tile, K-block) iterations are split evenly, worker w owning
-//    [w*T/W, (w+1)*T/W) cut at tile boundaries.  No SM idles in a partial
-//    last wave, and the concurrent tiles stay neighbours in the raster order
-//    (an all-stream-K walk spreads the workers over the whole tile range at
-//    once and loses L2 reuse).
+//    above, whole tiles in waves; the remaining tiles (a last wave at most
+//    half full, or else the last one to two waves' worth) form the stream-K
+//    region, whose T = (num_tiles - dp_tiles) * kb_total (tile, K-block)
+//    iterations are split evenly over the first W' = sk_workers workers,
+//    worker w owning [w*T/W', (w+1)*T/W') cut at tile boundaries.  A half
+//    empty last wave of R tiles takes W' = 2R: every tile in two K halves.
+//    No SM idles in a partial last wave, and the concurrent tiles stay
+//    neighbours in the raster order (an all-stream-K walk spreads the
+//    workers over the whole tile range at once and loses L2 reuse).
 struct WorkIter {
   long long cur, end;  // stream-K region / data-parallel unit index and limit
   int dp;              // stream-K mode: next data-parallel tile of this worker
@@ -188,8 +191,9 @@ __device__ __forceinline__ WorkIter work_begin(const GemmParams& p, int worker, 
   if (p.streamk) {
     const long long base = static_cast<long long>(p.dp_tiles) * p.kb_total;
     w.dp = worker;
-    w.cur = base + static_cast<long long>(worker) * p.total_iters / workers;
-    w.end = base + static_cast<long long>(worker + 1) * p.total_iters / workers;
+    const int sw = p.sk_workers;
+    w.cur = worker < sw ? base + static_cast<long long>(worker) * p.total_iters / sw : base;
+    w.end = worker < sw ? base + static_cast<long long>(worker + 1) * p.total_iters / sw : base;
   } else {
     w.dp = 0;
     w.cur = worker;
@@ -201,8 +205,8 @@ __device__ __forceinline__ WorkIter work_begin(const GemmParams& p, int worker, 
 
 // Worker that owns iteration x of the stream-K region (x counted from the
 // region's start).
-__device__ __forceinline__ int sk_owner(const GemmParams& p, long long x, int workers) {
-  return static_cast<int>(((x + 1) * workers - 1) / p.total_iters);
+__device__ __forceinline__ int sk_owner(const GemmParams& p, long long x) {
+  return static_cast<int>(((x + 1) * p.sk_workers - 1) / p.total_iters);
 }
 
 __device__ __forceinline__ bool work_next(const GemmParams& p, int worker, int workers, WorkIter& it, Unit& w) {
@@ -225,9 +229,9 @@ __device__ __forceinline__ bool work_next(const GemmParams& p, int worker, int w
     w.kb1 = (left < kbt - w.kb0) ? w.kb0 + static_cast<int>(left) : kbt;
     it.cur += w.kb1 - w.kb0;
     const long long t0 = static_cast<long long>(w.tile - p.dp_tiles) * kbt;
-    const int first = sk_owner(p, t0, workers);
+    const int first = sk_owner(p, t0);
     w.part = worker - first;
-    w.nparts = sk_owner(p, t0 + kbt - 1, workers) - first + 1;
+    w.nparts = sk_owner(p, t0 + kbt - 1) - first + 1;
     w.down = false;
   } else {
     const int u = static_cast<int>(it.cur);

@@ -143,3 +143,20 @@ def test_torch_binding_loads_and_checks_on_cpu():
         ext._fast.gemm_forward_cfg(A, A, 0)
     with pytest.raises(RuntimeError, match="A must be CUDA tensor"):
         ext._fast.gemm_ex(A, A, 0)
+
+
+def test_streamk_splits_only_a_half_empty_last_wave():
+    """256x256 pair tiles at 4096^3: 256 tiles on 74 pairs = 3 full waves + 34 tiles.  A last wave at most
+    half full is the whole stream-K region (the full waves run data-parallel), shared by 68 workers: each
+    of its tiles is cut into exactly two K halves, two partial slots per tile half."""
+    cnt = _capi.lib.gemm_workspace_counter_bytes()
+    aligned = 1 << 20
+    ks = (256, 256, 64, 6, 2, 1, 16, 0)
+    tiles, kbt, workers = 256, 64, 74
+    region = tiles - 3 * workers              # 34 tiles
+    assert _streamk_parts(region, kbt, 2 * region) == 2
+    assert _ws(aligned, aligned, 4096, 4096, 4096, 4096, 4096, ks) == cnt + tiles * 2 * 2 * 128 * 256 * 4
+    # a last wave more than half full (272 tiles: 3 waves + 50): the last full wave joins the region
+    region = 272 - 2 * workers                # 124 tiles
+    parts = _streamk_parts(region, kbt, workers)
+    assert _ws(aligned, aligned, 4096, 4352, 4096, 4096, 4352, ks) == cnt + 272 * 2 * parts * 128 * 256 * 4

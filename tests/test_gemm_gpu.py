@@ -84,21 +84,26 @@ def test_split_k(cuda_device, split_k):
 
 @pytest.mark.parametrize("M,N,K,tile_n", [(64, 4096, 4096, 128), (16, 14336, 4096, 256), (1, 4096, 4096, 64),
                                            (300, 700, 333, 128), (128, 148 * 128, 512, 128), (1000, 3000, 777, 192),
-                                           (513, 1000, 64, 64)])
+                                           (513, 1000, 64, 64), (1660, 1530, 700, 128)])
 def test_stream_k(cuda_device, M, N, K, tile_n):
     """split_k = 0: every CTA takes an equal share of all (tile, K-block) iterations."""
     _check(M, N, K, _cfg(tile_n, 4, 0, 8, 0), dist="skinny", seed=M + N + K)
 
 
 @pytest.mark.parametrize("M,N,K,tile_n", [(320, 704, 328, 128), (1100, 1536, 2048, 256), (100, 1000, 4096, 256),
-                                           (130, 3000, 1000, 128), (2048, 2048, 2048, 256), (4096, 1024, 4096, 256)])
+                                           (130, 3000, 1000, 128), (2048, 2048, 2048, 256), (4096, 1024, 4096, 256),
+                                           (1790, 3070, 520, 256)])
 def test_stream_k_pairs(cuda_device, M, N, K, tile_n):
-    """Stream-K on CTA pairs: each CTA of the pair reduces its own 128 rows (M=100: the odd CTA has none)."""
+    """Stream-K on CTA pairs: each CTA of the pair reduces its own 128 rows (M=100: the odd CTA has none).
+    1790 x 3070 (84 pair tiles: one full wave and 10 tiles) and 1660 x 1530 above (156 one-CTA tiles: 148 and
+    8) take the half-empty-last-wave walk: every full wave data-parallel, the last wave's tiles in two K
+    halves on twice as many workers."""
     _check(M, N, K, _cfg(tile_n, 4, 0, 8, 0, mma_sm=2), dist="skinny", seed=M + K)
 
 
 def test_stream_k_pairs_large_sampled_rows(cuda_device):
-    """4096^3 on stream-K pairs (256 tiles on 74 pairs: every tile split), oracle on sampled rows."""
+    """4096^3 on stream-K pairs (256 tiles on 74 pairs: three waves data-parallel, the last 34 tiles in two K
+    halves on 68 pairs), oracle on sampled rows."""
     n = 4096
     A, B = make_inputs(n, n, n, seed=7)
     C = capi_gemm(A.cuda(), B.cuda(), _cfg(256, 4, 1, 8, 0, mma_sm=2))
