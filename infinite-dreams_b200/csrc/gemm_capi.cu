@@ -66,6 +66,33 @@ static const SkinnyVariant kSkinnyVariants[] = {
 // Copies a row-major fp16 matrix into a buffer whose row pitch is a multiple
 // of 8 elements (16 bytes) so that TMA can address it.  Used only when a
 // caller's A or B pitch / base address is not 16-byte aligned.
+//
+// One thread writes one 16-byte chunk (8 elements) of the packed copy.  Its
+// source starts at a 2-byte aligned address, so it reads the one or two
+// aligned 16-byte chunks that cover it with vector loads and shifts the bytes
+// into place in registers (2-, 4- and 8-byte steps); neighbouring threads
+// read the same chunks, which the cache serves.  A chunk that would reach
+// outside the matrix's first and last bytes (its first or last 16 bytes, or
+// a row's ragged end) is read element by element instead, so no load leaves
+// the caller's memory.  Elements past `cols` in the last chunk of a row are
+// written as zero (the tensor map's extent excludes them anyway).
+__device__ __forceinline__ uint4 shift_chunks(uint4 c0, uint4 c1, int o) {
+  uint32_t w0 = c0.x, w1 = c0.y, w2 = c0.z, w3 = c0.w, w4 = c1.x, w5 = c1.y, w6 = c1.z, w7 = c1.w;
+  if (o & 8) {
+    w0 = w2; w1 = w3; w2 = w4; w3 = w5; w4 = w6; w5 = w7;
+  }
+  if (o & 4) {
+    w0 = w1; w1 = w2; w2 = w3; w3 = w4; w4 = w5;
+  }
+  if (o & 2) {  // bytes 2..3 of one word, then bytes 0..1 of the next
+    w0 = __byte_perm(w0, w1, 0x5432);
+    w1 = __byte_perm(w1, w2, 0x5432);
+    w2 = __byte_perm(w2, w3, 0x5432);
+    w3 = __byte_perm(w3, w4, 0x5432);
+  }
+  return make_uint4(w0, w1, w2, w3);
+}
+
 __global__ void pack_rows_f16(const __half* __restrict__ src, long long lds, __half* __restrict__ dst,
                               long long ldd, int rows, int cols) {
   // The GEMM that reads the packed copy is launched as a programmatic
@@ -74,20 +101,29 @@ __global__ void pack_rows_f16(const __half* __restrict__ src, long long lds, __h
   griddep_launch_dependents();
   const long long chunks = (cols + 7) / 8;
   const long long total = static_cast<long long>(rows) * chunks;
-  const unsigned short* s16 = reinterpret_cast<const unsigned short*>(src);
+  const uintptr_t begin = reinterpret_cast<uintptr_t>(src);
+  const uintptr_t end = begin + (static_cast<uintptr_t>(rows - 1) * static_cast<uintptr_t>(lds) + cols) * 2u;
   for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
        idx += static_cast<long long>(gridDim.x) * blockDim.x) {
     const long long r = idx / chunks;
     const int c = static_cast<int>(idx - r * chunks) * 8;
-    const unsigned short* sp = s16 + r * lds + c;
-    unsigned short v[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = (c + i < cols) ? sp[i] : static_cast<unsigned short>(0);
+    const uintptr_t a = begin + static_cast<uintptr_t>(r * lds + c) * 2u;
+    const uintptr_t lo = a & ~static_cast<uintptr_t>(15);
+    const int o = static_cast<int>(a - lo);
     uint4 w;
-    w.x = v[0] | (static_cast<unsigned>(v[1]) << 16);
-    w.y = v[2] | (static_cast<unsigned>(v[3]) << 16);
-    w.z = v[4] | (static_cast<unsigned>(v[5]) << 16);
-    w.w = v[6] | (static_cast<unsigned>(v[7]) << 16);
+    if (c + 8 <= cols && lo >= begin && lo + (o ? 32u : 16u) <= end) {
+      const uint4 c0 = __ldg(reinterpret_cast<const uint4*>(lo));
+      w = o ? shift_chunks(c0, __ldg(reinterpret_cast<const uint4*>(lo + 16)), o) : c0;
+    } else {
+      const unsigned short* sp = reinterpret_cast<const unsigned short*>(a);
+      unsigned short v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = (c + i < cols) ? sp[i] : static_cast<unsigned short>(0);
+      w.x = v[0] | (static_cast<unsigned>(v[1]) << 16);
+      w.y = v[2] | (static_cast<unsigned>(v[3]) << 16);
+      w.z = v[4] | (static_cast<unsigned>(v[5]) << 16);
+      w.w = v[6] | (static_cast<unsigned>(v[7]) << 16);
+    }
     *reinterpret_cast<uint4*>(dst + r * ldd + c) = w;
   }
 }

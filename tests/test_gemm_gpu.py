@@ -222,3 +222,29 @@ def test_torch_op_surface(cuda_device):
     with pytest.raises(RuntimeError, match="cfg_id out of range"):
         ext.gemm_forward_cfg(Ad, Bd, ext.NUM_CFG)
     ext.check_device_errors()
+
+
+def _placed(X, shift, pitch):
+    """X copied into a flat device buffer at element offset `shift` with row pitch `pitch`; the buffer ends
+    exactly at X's last element, so no row is followed by anything of the buffer."""
+    rows, cols = X.shape
+    flat = torch.full((shift + (rows - 1) * pitch + cols,), float("nan"), dtype=torch.float16, device="cuda")
+    view = flat.as_strided((rows, cols), (pitch, 1), shift)
+    view.copy_(X.cuda())
+    return view
+
+
+@pytest.mark.parametrize("shift_a,pad_a,shift_b,pad_b", [(1, 1, 0, 0), (3, 5, 2, 7), (0, 0, 5, 3), (7, 1, 1, 1),
+                                                         (2, 0, 6, 0), (4, 2, 0, 8)])
+def test_repack_bit_identical_to_aligned(cuda_device, shift_a, pad_a, shift_b, pad_b):
+    """Operands whose base or pitch TMA cannot address are repacked (aligned 16-byte loads shifted into place,
+    element loads at the matrix's edges) before the GEMM: every 2-byte misalignment of the base, odd pitches,
+    and matrices that end at the end of their buffer give the same bits as the aligned operands."""
+    M, N, K = 333, 1000, 776
+    A, B = make_inputs(M, N, K, seed=shift_a * 10 + shift_b)
+    cid = _cfg(128, 4, 0, 8, 1)
+    aligned = capi_gemm(A.cuda(), B.cuda(), cid)
+    Ad = _placed(A, shift_a, K + pad_a)
+    Bd = _placed(B, shift_b, N + pad_b)
+    got = capi_gemm(Ad, Bd, cid, lda=K + pad_a, ldb=N + pad_b, M=M, N=N, K=K)
+    assert torch.equal(got.view(torch.int16), aligned.view(torch.int16)), (shift_a, pad_a, shift_b, pad_b)
