@@ -846,12 +846,12 @@ def shapes_block(args: argparse.Namespace, pk: Dict[str, object]) -> Dict[str, o
                    "ms_graph_b2b: back to back replayed from a CUDA graph; ms_torch_cublas: torch.matmul timed "
                    "like ms"),
         "roofline": ("pct_roofline_measured = max(2MNK/bf16 burst peak, 2(MK+KN+MN)/HBM copy rate) / ms, "
-                     "measured peaks of this box"),
+                     "measured peaks of this box; pct_roofline_measured_graph: the same over ms_graph_b2b"),
         "rows": [],
     }
     keep = ("set", "M", "N", "K", "cfg_id", "knobs", "bound", "ms", "ms_warm_b2b", "ms_graph_b2b",
             "ms_torch_cublas", "tflops", "gbs", "pct_fp16_peak_nominal", "pct_roofline_nominal",
-            "pct_roofline_measured", "parity")
+            "pct_roofline_measured", "pct_roofline_measured_graph", "parity")
     for r in rows:
         e = {k: r.get(k) for k in keep}
         e["knobs"] = list(r["knobs"].values())

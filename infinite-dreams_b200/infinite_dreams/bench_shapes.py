@@ -139,6 +139,9 @@ def run(sets: List[str], iters: int, warmup: int, cfg_override: Optional[int] = 
                 "pct_fp16_peak_nominal": 100.0 * flops / (ms * 1e-3) / 1e12 / NOMINAL_TFLOPS,
                 "pct_roofline_nominal": 100.0 * roofline_ms(M, N, K, NOMINAL_TFLOPS, NOMINAL_GBS) / ms,
                 "pct_roofline_measured": 100.0 * roofline_ms(M, N, K, mp["tflops"], mp["gbs"]) / ms,
+                # the same against the back-to-back time replayed from a CUDA graph: device time per
+                # launch in a stream of launches, without the one launch's latency
+                "pct_roofline_measured_graph": 100.0 * roofline_ms(M, N, K, mp["tflops"], mp["gbs"]) / ms_graph,
                 "bound": "tensor" if flops / (NOMINAL_TFLOPS * 1e12) > nbytes / (NOMINAL_GBS * 1e9) else "hbm",
             })
             if parity is not None:
