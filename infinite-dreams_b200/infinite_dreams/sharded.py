@@ -303,9 +303,14 @@ class OverlappedGather:
        has issued its reads of the result of step i-2, which lives in the
        same buffer;
     2. the copy engines copy this rank's rows (one contiguous block) into
-       every peer's buffer, one copy stream per peer;
+       every peer's buffer, one copy stream per peer -- or, with
+       ``pull=True``, copy every peer's rows from its buffer into this
+       rank's;
     3. the flags go to 2i+2 the same way: every rank's copies of step i are
-       done, so this rank's buffer holds the whole C of step i.
+       done, so every buffer holds the whole C of step i (with ``pull``,
+       this rank's buffer is complete after its own copies, and the flags
+       say that every rank has read this rank's rows, which the step after
+       next overwrites).
 
     The GEMM of step i+1 runs while the copies of step i proceed.  The flag
     writes and waits are stream memory operations, executed by the GPU's
@@ -320,9 +325,11 @@ class OverlappedGather:
     memory.
     """
 
-    def __init__(self, rows: int, N: int, K: int, device: torch.device, group=None, cfg_id: Optional[int] = None):
+    def __init__(self, rows: int, N: int, K: int, device: torch.device, group=None, cfg_id: Optional[int] = None,
+                 pull: bool = False):
         from . import _capi, dispatch
 
+        self.pull = pull
         self.group = group
         self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
         if self.world - 1 > _capi.GEMM_MAX_PEERS:
@@ -400,25 +407,39 @@ class OverlappedGather:
         self._barrier(s0, 2 * i + 1)
         started = torch.cuda.Event()
         started.record(s0)
-        offset = self.rank * self.rows * self.N * 2
         nbytes = self.rows * self.N * 2
-        targets = [p for p in peers if p is not None]
-        for k, base in enumerate(targets):
+        others = [(r, p) for r, p in enumerate(peers) if p is not None]
+        for k, (r, base) in enumerate(others):
             s = self.streams[k]
             if k:
                 s.wait_event(started)
-            _capi.check(_capi.lib.gemm_ipc_copy(base + offset, mine.data_ptr(), nbytes, s.cuda_stream),
-                        "gemm_ipc_copy")
-        for s in self.streams[1:len(targets)]:
+            if self.pull:
+                # rank r's rows, from its buffer into the same place of this rank's
+                off = r * nbytes
+                _capi.check(_capi.lib.gemm_ipc_copy(full.data_ptr() + off, base + off, nbytes, s.cuda_stream),
+                            "gemm_ipc_copy")
+            else:
+                # this rank's rows into rank r's buffer
+                off = self.rank * nbytes
+                _capi.check(_capi.lib.gemm_ipc_copy(base + off, mine.data_ptr(), nbytes, s.cuda_stream),
+                            "gemm_ipc_copy")
+        for s in self.streams[1:len(others)]:
             ev = torch.cuda.Event()
             ev.record(s)
             s0.wait_event(ev)
-        copied = torch.cuda.Event()
-        copied.record(s0)
-        self.copied[b] = copied
-        self._barrier(s0, 2 * i + 2)
         done = torch.cuda.Event()
-        done.record(s0)
+        copied = torch.cuda.Event()
+        if self.pull:
+            # this rank's buffer is complete once its own pulls are; its rows
+            # may be overwritten only once every rank has pulled them
+            done.record(s0)
+            self._barrier(s0, 2 * i + 2)
+            copied.record(s0)
+        else:
+            copied.record(s0)
+            self._barrier(s0, 2 * i + 2)
+            done.record(s0)
+        self.copied[b] = copied
         return GatherResult(full, done)
 
     def close(self) -> None:

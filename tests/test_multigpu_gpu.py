@@ -59,13 +59,14 @@ def _worker(rank, world, port, M, N, K, q):
             from infinite_dreams.sharded import OverlappedGather
             A2, _ = make_inputs(M, N, K, seed=6)
             A2_local = A2[r0:r1].contiguous().to(dev)
-            og = OverlappedGather(r1 - r0, N, K, dev)
-            for s in range(4):
-                res = og.step(A_local if s % 2 == 0 else A2_local, Bd)
-                full = res.wait()
-                torch.cuda.synchronize()
-                fused.append(("overlapped", s % 2, full.cpu().numpy().view(np.uint16).copy()))
-            og.close()
+            for pull in (False, True):
+                og = OverlappedGather(r1 - r0, N, K, dev, pull=pull)
+                for s in range(4):
+                    res = og.step(A_local if s % 2 == 0 else A2_local, Bd)
+                    full = res.wait()
+                    torch.cuda.synchronize()
+                    fused.append(("overlapped", s % 2, full.cpu().numpy().view(np.uint16).copy()))
+                og.close()
         else:
             try:
                 sharded_gemm(A_local, Bd, M_total=M, gather=True, exchange="fused")
@@ -111,7 +112,7 @@ def test_sharded_gemm_nccl_allgather(cuda_device, M):
             g = f.view(np.float16).astype(np.float32)
             assert g.shape == ref.shape and np.isfinite(g).all(), rank
             assert np.abs(g - refs[which]).max() <= tol, ("fused / overlapped", rank, which)
-        assert len(fused) == (7 if M % world == 0 else 0)
+        assert len(fused) == (11 if M % world == 0 else 0)
 
 
 def _worker_large(rank, world, port, S, q):
