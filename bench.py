@@ -656,7 +656,7 @@ def time_exchange(args, A, B, C, step, cfg_id, size, rows, N, world, dev, stream
     import torch.distributed as dist
 
     from infinite_dreams import dispatch, infinite_dreams_ext as ext
-    from infinite_dreams.sharded import OverlappedGather, release_peer_buffers, sharded_gemm
+    from infinite_dreams.sharded import release_peer_buffers, sharded_gemm
 
     Cfull = torch.empty((size, N), device=dev, dtype=torch.float16)
     n_ag = max(1, min(args.steps, 20))
@@ -707,37 +707,13 @@ def time_exchange(args, A, B, C, step, cfg_id, size, rows, N, world, dev, stream
     ms_fused = timed(fused)
     check("fused_allgather", fused_out[0])
     fused_out.clear()
-    # Back-to-back steps whose all-gathers (copy engines) overlap the next
-    # step's GEMM: the timed region ends when the last step's C is complete
-    # on every rank.
-    og = OverlappedGather(rows, N, size, dev, cfg_id=cfg_id)
-    for _ in range(2):
-        og.step(A, B)
-    barrier()
-    s0 = torch.cuda.Event(enable_timing=True)
-    s1 = torch.cuda.Event(enable_timing=True)
-    s0.record(stream)
-    res = None
-    for _ in range(n_ag):
-        res = og.step(A, B)
-    res.wait(stream)
-    s1.record(stream)
-    torch.cuda.synchronize()
-    t = torch.tensor([s0.elapsed_time(s1)], device=dev, dtype=torch.float64)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_ovl = float(t[0]) / n_ag
-    check("overlapped_steps_allgather", res.full)
-    og.close()
     flop = 2.0 * size ** 3
     out = {"ms_per_step_gemm_then_allgather": ms_one, "value_gemm_then_allgather": flop / (ms_one * 1e-3) / 1e12,
            "ms_per_step_pipelined_2_chunks": ms_pipe, "value_pipelined": flop / (ms_pipe * 1e-3) / 1e12,
            "ms_per_step_fused": ms_fused, "value_fused": flop / (ms_fused * 1e-3) / 1e12,
-           "ms_per_step_overlapped": ms_ovl, "value_overlapped": flop / (ms_ovl * 1e-3) / 1e12,
            "bytes_received_per_rank": (world - 1) * rows * N * 2, "steps": n_ag,
            "note": ("each rank ends every step with the whole 16384x16384 C; times are max over ranks. fused: the "
-                    "kernel's epilogue stores every tile into every rank's C over NVLink; overlapped: back-to-back "
-                    "steps, each rank's C block copied to every peer by the copy engines while the next step's "
-                    "GEMM runs (ranks ordered by stream-ordered flags), timed until the last step's C is complete")}
+                    "kernel's epilogue stores every tile into every rank's C over NVLink (TMA stores)")}
     del Cfull
     release_peer_buffers()
     return out

@@ -152,27 +152,6 @@ int gemm_ipc_export(const void* ptr, void* handle, int64_t* offset);
 int gemm_ipc_import(const void* handle, int64_t offset, void** ptr);
 int gemm_ipc_close(void* ptr);
 
-/* Stream-ordered helpers for exchanges that must not occupy SMs (the
- * overlapped all-gather of back-to-back sharded GEMMs, where a persistent
- * GEMM holds every SM while the previous step's result moves):
- *   gemm_ipc_copy       bytes from src to dst on `stream` by the copy
- *                       engines (either side may be a gemm_ipc_import
- *                       mapping of another GPU's memory);
- *   gemm_stream_signal  writes `value` to the 32-bit word `flag` (local or
- *                       mapped peer memory) once earlier work on `stream`
- *                       is done;
- *   gemm_stream_wait    holds later work on `stream` until the word at
- *                       `flag` is >= `value` (compared as a wrapping
- *                       32-bit difference).
- * The signal and the wait are executed by the GPU's front end, not by a
- * kernel.  A wait on a flag that nothing will write holds its stream until
- * the process exits: a caller that signals from other processes must keep
- * every process's signals in the same order.  No counterpart in the
- * reference. */
-int gemm_ipc_copy(void* dst, const void* src, size_t bytes, void* stream);
-int gemm_stream_signal(void* stream, void* flag, uint32_t value);
-int gemm_stream_wait(void* stream, const void* flag, uint32_t value);
-
 /* A reasonable configuration for a shape when no tuned entry exists.
  * No counterpart in the reference (its tuner had no per-shape dispatch). */
 int gemm_default_cfg(int64_t M, int64_t N, int64_t K);

@@ -848,50 +848,6 @@ int gemm_ipc_close(void* ptr) {
   return e == cudaSuccess ? GEMM_OK : fail_cuda(e, "cudaIpcCloseMemHandle");
 }
 
-namespace {
-
-using StreamValueFn = CUresult (*)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
-
-StreamValueFn stream_value_fn(const char* name) {
-  void* f = nullptr;
-  cudaDriverEntryPointQueryResult q;
-  if (cudaGetDriverEntryPoint(name, &f, cudaEnableDefault, &q) != cudaSuccess || q != cudaDriverEntryPointSuccess) {
-    return nullptr;
-  }
-  return reinterpret_cast<StreamValueFn>(f);
-}
-
-}  // namespace
-
-int gemm_ipc_copy(void* dst, const void* src, size_t bytes, void* stream) {
-  t_last_error.clear();
-  if (bytes == 0) return GEMM_OK;
-  if (!dst || !src) return fail(GEMM_ERR_INVALID_ARG, "dst and src must be non-null");
-  cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, static_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? GEMM_OK : fail_cuda(e, "cudaMemcpyAsync");
-}
-
-int gemm_stream_signal(void* stream, void* flag, uint32_t value) {
-  t_last_error.clear();
-  static StreamValueFn fn = stream_value_fn("cuStreamWriteValue32");
-  if (!fn) return fail(GEMM_ERR_CUDA, "cuStreamWriteValue32 is not available from the driver");
-  if (!flag || reinterpret_cast<uintptr_t>(flag) % 4u) return fail(GEMM_ERR_INVALID_ARG, "flag must be 4-byte aligned");
-  CUresult r = fn(static_cast<CUstream>(stream), reinterpret_cast<CUdeviceptr>(flag), value,
-                  CU_STREAM_WRITE_VALUE_DEFAULT);
-  return r == CUDA_SUCCESS ? GEMM_OK
-                           : fail(GEMM_ERR_CUDA, "cuStreamWriteValue32 failed with CUresult " + std::to_string(r));
-}
-
-int gemm_stream_wait(void* stream, const void* flag, uint32_t value) {
-  t_last_error.clear();
-  static StreamValueFn fn = stream_value_fn("cuStreamWaitValue32");
-  if (!fn) return fail(GEMM_ERR_CUDA, "cuStreamWaitValue32 is not available from the driver");
-  if (!flag || reinterpret_cast<uintptr_t>(flag) % 4u) return fail(GEMM_ERR_INVALID_ARG, "flag must be 4-byte aligned");
-  CUresult r = fn(static_cast<CUstream>(stream), reinterpret_cast<CUdeviceptr>(flag), value, CU_STREAM_WAIT_VALUE_GEQ);
-  return r == CUDA_SUCCESS ? GEMM_OK
-                           : fail(GEMM_ERR_CUDA, "cuStreamWaitValue32 failed with CUresult " + std::to_string(r));
-}
-
 int gemm_launch_knobs(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
                       int64_t ldb, int64_t ldc, const int* knobs, int n, void* workspace, size_t workspace_bytes,
                       void* stream) {

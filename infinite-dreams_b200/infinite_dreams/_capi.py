@@ -56,9 +56,6 @@ _SIG = [
     ("gemm_ipc_export", ctypes.c_int, [_P, _P, ctypes.POINTER(ctypes.c_int64)]),
     ("gemm_ipc_import", ctypes.c_int, [_P, _I64, ctypes.POINTER(ctypes.c_void_p)]),
     ("gemm_ipc_close", ctypes.c_int, [_P]),
-    ("gemm_ipc_copy", ctypes.c_int, [_P, _P, ctypes.c_size_t, _P]),
-    ("gemm_stream_signal", ctypes.c_int, [_P, _P, ctypes.c_uint32]),
-    ("gemm_stream_wait", ctypes.c_int, [_P, _P, ctypes.c_uint32]),
     ("gemm_default_cfg", ctypes.c_int, [_I64, _I64, _I64]),
     ("gemm_device_error", ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
     ("gemm_selftest_wait_timeout", ctypes.c_int, [ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64)]),

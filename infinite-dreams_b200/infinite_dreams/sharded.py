@@ -20,14 +20,6 @@ the remaining tiles' mainloop.  A one-element NCCL all-reduce issued after
 the launch on the same stream marks the point where every rank's grid, and
 with it every write into this rank's C, has completed.  No kernel reads
 another GPU's memory; peers are only written to.
-
-``OverlappedGather`` runs back-to-back GEMMs of one shape and overlaps each
-step's all-gather with the next step's GEMM: once a rank's GEMM has
-finished, copy streams move its row block into every other rank's C with the
-copy engines (one contiguous block per peer over NVLink), while the next
-GEMM computes.  Remote stores issued by the SMs share the SMs' path to
-memory with the GEMM's own operand loads, and when the links are busy the
-loads queue behind them; the copy engines keep that traffic off the SMs.
 """
 from __future__ import annotations
 
@@ -271,191 +263,6 @@ def _fused_gather(A_local: torch.Tensor, B: torch.Tensor, M_total: Optional[int]
         done = torch.zeros(1, dtype=torch.float32, device=device)
         dist.all_reduce(done, group=group)
     return full
-
-
-class GatherResult:
-    """The whole C of one OverlappedGather step on this rank."""
-
-    def __init__(self, full: torch.Tensor, done: torch.cuda.Event):
-        self.full = full
-        self._done = done
-
-    def wait(self, stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
-        """Makes `stream` (default: the current stream) wait until every
-        rank's rows of this step are in ``full``; returns ``full``."""
-        (stream or torch.cuda.current_stream(self.full.device)).wait_event(self._done)
-        return self.full
-
-
-class OverlappedGather:
-    """Back-to-back sharded GEMMs of one shape, each step's all-gather of C
-    overlapping the next step's GEMM.
-
-    Every rank holds two full-size C buffers, used by alternate steps, which
-    the other ranks map (CUDA IPC), and a small array of step flags, which
-    they map too.  ``step(A_local, B)`` launches this rank's GEMM into its
-    rows of the step's buffer on the calling stream; then, on side streams
-    and without any kernel:
-
-    1. once the GEMM is done, this rank's flag in every peer's array is set
-       to 2i+1 and the side stream waits until every peer has set its flag
-       here to 2i+1 -- every rank's GEMM of step i is done, so every rank
-       has issued its reads of the result of step i-2, which lives in the
-       same buffer;
-    2. the copy engines copy this rank's rows (one contiguous block) into
-       every peer's buffer, one copy stream per peer -- or, with
-       ``pull=True``, copy every peer's rows from its buffer into this
-       rank's;
-    3. the flags go to 2i+2 the same way: every rank's copies of step i are
-       done, so every buffer holds the whole C of step i (with ``pull``,
-       this rank's buffer is complete after its own copies, and the flags
-       say that every rank has read this rank's rows, which the step after
-       next overwrites).
-
-    The GEMM of step i+1 runs while the copies of step i proceed.  The flag
-    writes and waits are stream memory operations, executed by the GPU's
-    front end, so they need no SM while a persistent GEMM holds all of them
-    (a collective would, and would start only after that GEMM).  Every rank
-    must call ``step`` the same number of times.
-
-    ``step`` returns a ``GatherResult``: ``wait()`` orders the calling
-    stream after the step's exchange.  The buffer stays intact until the
-    step after next is called, so reads of it must be issued (after
-    ``wait()``) before then.  ``close()`` (collective) unmaps the peers'
-    memory.
-    """
-
-    def __init__(self, rows: int, N: int, K: int, device: torch.device, group=None, cfg_id: Optional[int] = None,
-                 pull: bool = False):
-        from . import _capi, dispatch
-
-        self.pull = pull
-        self.group = group
-        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
-        if self.world - 1 > _capi.GEMM_MAX_PEERS:
-            raise ValueError(f"OverlappedGather supports at most {_capi.GEMM_MAX_PEERS + 1} ranks")
-        if not _equal_rows(rows, device, group):
-            raise ValueError("OverlappedGather needs equal row blocks on every rank")
-        self.rows, self.N, self.K, self.device = rows, N, K, device
-        self.cfg_id = dispatch.lookup(rows, N, K) if cfg_id is None else cfg_id
-        # Two buffers of the whole C; the first one carries the step flags
-        # after its C: flags[r] is the last stage that rank r reported here.
-        c_bytes = rows * self.world * N * 2
-        self._raw = [torch.zeros(c_bytes + (4096 if j == 0 else 0), dtype=torch.uint8, device=device)
-                     for j in range(2)]
-        self.flags = self._raw[0][c_bytes:c_bytes + 4 * 64].view(torch.int32)
-        self.bufs = []
-        for raw in self._raw:
-            full = raw[:c_bytes].view(torch.float16).view(rows * self.world, N)
-            self.bufs.append((full, self._map_peers(raw)))
-        self.peer_flags = [None if p is None else p + c_bytes for p in self.bufs[0][1]]
-        self.streams = [torch.cuda.Stream(device) for _ in range(max(1, self.world - 1))]
-        self.copied: List[Optional[torch.cuda.Event]] = [None, None]
-        self.i = 0
-
-    def _map_peers(self, raw: torch.Tensor) -> List[Optional[int]]:
-        """Every other rank's counterpart of `raw`, mapped into this process."""
-        from . import _capi
-
-        handle = (ctypes.c_char * _capi.GEMM_IPC_HANDLE_BYTES)()
-        offset = ctypes.c_int64(0)
-        _capi.check(_capi.lib.gemm_ipc_export(raw.data_ptr(), handle, ctypes.byref(offset)), "gemm_ipc_export")
-        shared: List[Optional[Tuple[bytes, int]]] = [None] * self.world
-        torch.cuda.synchronize(self.device)   # the zeroed flags are in memory before any peer maps them
-        dist.all_gather_object(shared, (bytes(handle), offset.value), group=self.group)
-        out: List[Optional[int]] = []
-        for r, (h, off) in enumerate(shared):
-            if r == self.rank:
-                out.append(None)
-                continue
-            ptr = ctypes.c_void_p()
-            _capi.check(_capi.lib.gemm_ipc_import(h, off, ctypes.byref(ptr)), "gemm_ipc_import")
-            out.append(int(ptr.value))
-        return out
-
-    def _barrier(self, s: torch.cuda.Stream, value: int) -> None:
-        """Tells every peer (on stream s) that this rank reached `value`, then
-        holds s until every peer has reached it too."""
-        from . import _capi
-
-        lib = _capi.lib
-        for r, base in enumerate(self.peer_flags):
-            if base is not None:
-                _capi.check(lib.gemm_stream_signal(s.cuda_stream, base + 4 * self.rank, value), "gemm_stream_signal")
-        for r in range(self.world):
-            if r != self.rank:
-                _capi.check(lib.gemm_stream_wait(s.cuda_stream, self.flags.data_ptr() + 4 * r, value),
-                            "gemm_stream_wait")
-
-    def step(self, A_local: torch.Tensor, B: torch.Tensor) -> GatherResult:
-        from . import _capi, infinite_dreams_ext as ext
-
-        if tuple(A_local.shape) != (self.rows, self.K) or tuple(B.shape) != (self.K, self.N):
-            raise ValueError("OverlappedGather.step: A_local must be rows x K and B K x N, as constructed")
-        i, b = self.i, self.i % 2
-        self.i += 1
-        full, peers = self.bufs[b]
-        mine = full[self.rank * self.rows:(self.rank + 1) * self.rows]
-        stream = torch.cuda.current_stream(self.device)
-        if self.copied[b] is not None:
-            stream.wait_event(self.copied[b])       # this rank's copies of step i-2 read these rows
-        ext.gemm_forward_cfg(A_local, B, self.cfg_id, out=mine)
-        computed = torch.cuda.Event()
-        computed.record(stream)
-        s0 = self.streams[0]
-        s0.wait_event(computed)
-        self._barrier(s0, 2 * i + 1)
-        started = torch.cuda.Event()
-        started.record(s0)
-        nbytes = self.rows * self.N * 2
-        others = [(r, p) for r, p in enumerate(peers) if p is not None]
-        for k, (r, base) in enumerate(others):
-            s = self.streams[k]
-            if k:
-                s.wait_event(started)
-            if self.pull:
-                # rank r's rows, from its buffer into the same place of this rank's
-                off = r * nbytes
-                _capi.check(_capi.lib.gemm_ipc_copy(full.data_ptr() + off, base + off, nbytes, s.cuda_stream),
-                            "gemm_ipc_copy")
-            else:
-                # this rank's rows into rank r's buffer
-                off = self.rank * nbytes
-                _capi.check(_capi.lib.gemm_ipc_copy(base + off, mine.data_ptr(), nbytes, s.cuda_stream),
-                            "gemm_ipc_copy")
-        for s in self.streams[1:len(others)]:
-            ev = torch.cuda.Event()
-            ev.record(s)
-            s0.wait_event(ev)
-        done = torch.cuda.Event()
-        copied = torch.cuda.Event()
-        if self.pull:
-            # this rank's buffer is complete once its own pulls are; its rows
-            # may be overwritten only once every rank has pulled them
-            done.record(s0)
-            self._barrier(s0, 2 * i + 2)
-            copied.record(s0)
-        else:
-            copied.record(s0)
-            self._barrier(s0, 2 * i + 2)
-            done.record(s0)
-        self.copied[b] = copied
-        return GatherResult(full, done)
-
-    def close(self) -> None:
-        """Collective: waits for outstanding work, unmaps the peers' memory,
-        and frees this rank's buffers once no rank has them mapped."""
-        from . import _capi
-
-        torch.cuda.synchronize(self.device)
-        for _, peers in self.bufs:
-            for ptr in peers:
-                if ptr is not None:
-                    _capi.check(_capi.lib.gemm_ipc_close(ptr), "gemm_ipc_close")
-        self.bufs, self.peer_flags = [], []
-        dist.barrier(group=self.group)
-        self._raw = []
-        self.flags = None
 
 
 def release_peer_buffers(group=None) -> None:
