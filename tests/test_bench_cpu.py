@@ -27,3 +27,73 @@ def test_sampled_rows_cover_every_block_edge():
             assert b[0] == r * rows and b[-1] == (r + 1) * rows - 1
             assert all(r * rows <= g < (r + 1) * rows for g in b) and b == sorted(set(b))
         assert sum(len(b) for b in blocks) >= 16
+
+
+def _parity_worker(rank, world, port, q):
+    """One gloo rank: its RowChecker against oracle-computed C blocks, one rank planting an error."""
+    import os
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parent.parent
+    for p in (str(root), str(root / "infinite-dreams_b200")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import bench
+    import oracle
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        S = 256
+        rows = S // world
+
+        def block(r):
+            g = torch.Generator().manual_seed(100 + r)
+            return (torch.rand((rows, S), generator=g) * 2 - 1).half()
+
+        B = (torch.rand((S, S), generator=torch.Generator().manual_seed(7)) * 2 - 1).half()
+        checker = bench.RowChecker(block, B, world, rank, S, threads=1)
+        full = np.concatenate([oracle.gemm_f16(block(r).numpy(), B.numpy()) for r in range(world)], 0)
+        full = torch.from_numpy(full)
+        mine = full[rank * rows:(rank + 1) * rows].clone()
+        checks = {"local": checker.check_local(mine), "full": checker.check_full(full)}
+        if rank == 1:
+            bad = full.clone()
+            bad[rows + 0, 5] += 1000.0      # rank 1's first row: always sampled
+            checks["planted"] = checker.check_full(bad)
+        else:
+            checks["planted"] = checker.check_full(full)
+        summary = bench._parity_summary(checks, checker, world, torch.device("cpu"))
+        q.put((rank, summary))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_parity_summary_combines_every_rank_with_gloo():
+    """The bench's oracle checks on two gloo ranks: correct blocks pass everywhere, and an error that only
+    rank 1 sees fails the combined result on every rank."""
+    import socket
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_parity_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, summary in results.items():
+        assert summary["ok"] is False, rank                      # the planted error reaches every rank
+        assert summary["checks"]["local"]["ok"] and summary["checks"]["full"]["ok"], (rank, summary)
+        assert not summary["checks"]["planted"]["ok"], (rank, summary)
+        assert summary["rows_checked_per_gathered_c"] >= 16
