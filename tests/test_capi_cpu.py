@@ -63,9 +63,9 @@ def test_workspace_sizing():
     # split larger than the number of K blocks is clamped (K=128: 2 blocks)
     k16 = (128, 128, 64, 4, 1, 0, 8, 16)
     assert _ws(aligned, aligned, 64, 512, 128, 128, 512, k16) == cnt + 4 * 2 * 128 * 128 * 4
-    # unaligned pitch of A (K=777): repacked into the workspace with pitch 784
+    # unaligned pitch of A (K=777): repacked into the workspace with pitch 832 (64-element rows)
     ws = _ws(aligned, aligned, 1000, 3000, 777, 777, 3000, k1)
-    assert ws == cnt + ((1000 * 784 * 2 + 255) // 256) * 256
+    assert ws == cnt + ((1000 * 832 * 2 + 255) // 256) * 256
     # unaligned base address of B
     ws = _ws(aligned, aligned + 2, 64, 64, 64, 64, 64, k1)
     assert ws == cnt + 64 * 64 * 2
