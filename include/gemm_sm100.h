@@ -128,8 +128,11 @@ size_t gemm_workspace_bytes_ex(const void* A, const void* B, int64_t M, int64_t 
  * process per GPU).  Same as gemm_launch, and each finished tile of C is
  * also stored, over NVLink, at the same offset and pitch ldc into
  * peer_C[0..n_peers) -- the copies of the full C on the other GPUs (opened
- * with gemm_ipc_import), already offset to this rank's rows.  The transfer
- * overlaps the GEMM tile by tile.  The caller learns that every peer has
+ * with gemm_ipc_import), already offset to this rank's rows.  When C and
+ * every peer copy are TMA-addressable, each staged box goes to the peers by
+ * TMA stores beside the local one; otherwise the epilogue warps copy it
+ * with 16-byte stores.  The transfer overlaps the GEMM tile by tile.  The
+ * caller learns that every peer has
  * finished writing into its own C from a collective issued after the
  * launch on the same stream (the stream orders it after this grid on every
  * rank).  n_peers <= GEMM_MAX_PEERS; the configuration must have
