@@ -123,6 +123,7 @@ class ClockSampler:
         self.bits: List[Tuple[float, int]] = []    # (t, raw NVML clock event reason mask)
         self.max_mhz: Optional[float] = None
         self.source = "none"
+        self.power_kind = "1 s average"
         self._stop = threading.Event()
         self._thread: Optional[threading.Thread] = None
         self._proc: Optional[subprocess.Popen] = None
@@ -162,14 +163,32 @@ class ClockSampler:
         self._thread = threading.Thread(target=self._read_smi, daemon=True)
         self._thread.start()
 
+    @staticmethod
+    def _instant_watts(h) -> Optional[float]:
+        """Instantaneous board power (NVML field), or None where the driver
+        does not offer it; the plain power reading is a ~1 s average, which
+        lags a short timed region."""
+        import pynvml
+
+        try:
+            v = pynvml.nvmlDeviceGetFieldValues(h, [pynvml.NVML_FI_DEV_POWER_INSTANT])[0]
+            if v.nvmlReturn != pynvml.NVML_SUCCESS:
+                return None
+            return float(v.value.uiVal) / 1000.0
+        except Exception:
+            return None
+
     def _poll_nvml(self, h) -> None:
         import pynvml
 
+        instant = self._instant_watts(h) is not None
+        self.power_kind = "instantaneous" if instant else "1 s average"
         while not self._stop.is_set():
             try:
                 t = time.monotonic()
                 mhz = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
-                watts = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+                w = self._instant_watts(h) if instant else None
+                watts = w if w is not None else pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
                 bits = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(h))
                 self.samples.append((t, mhz, watts, [n for b, n in _REASONS.items() if bits & b]))
                 self.bits.append((t, bits))
@@ -214,7 +233,7 @@ class ClockSampler:
         out = {"sm_mhz": mhz, "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(inside),
                "window_ms": (t1 - t0) * 1e3, "sm_mhz_min": min(s[1] for s in inside),
                "power_w_median": statistics.median(s[2] for s in inside),
-               "power_w_max": max(s[2] for s in inside), "sampler": self.source,
+               "power_w_max": max(s[2] for s in inside), "power_reading": self.power_kind, "sampler": self.source,
                "reason_samples": {r: sum(1 for s in inside if r in s[3]) for r in reasons}}
         masks = {b for t, b in self.bits if t0 <= t <= t1}
         if masks:
