@@ -10,8 +10,11 @@ A "step" is one GEMM over the local row block.
 At N > 1 the output exchange (all-gather of the C row blocks, so that every
 rank ends with the whole C) is timed after the GEMM loop and reported under
 "allgather": a GEMM followed by one NCCL all-gather, a two-chunk pipeline of
-both, and the exchange fused into the GEMM (every tile stored into every
-rank's C over NVLink from the epilogue).  Every result -- the local C block
+both, the exchange fused into the GEMM (every tile stored into every rank's
+C over NVLink from the epilogue), and, where the GPUs offer NVLink
+multicast, the fused exchange through NVSwitch multicast (every tile stored
+once, with multimem.st, and written by the switch into every rank's C).
+Every result -- the local C block
 and each gathered C -- is checked outside the timed regions on sampled rows
 against the oracle (the CPU restatement of the reference kernel) under
 |err| <= 1e-2*sqrt(K/1024)*max|C_ref| + 1e-3; "parity" in the line is true
@@ -669,13 +672,14 @@ def run_ours(args: argparse.Namespace) -> None:
 
 def time_exchange(args, A, B, C, step, cfg_id, size, rows, N, world, dev, stream, barrier, checker,
                   checks) -> Dict[str, object]:
-    """GEMM + all-gather of C, three ways; each timed over the same number of
-    steps (max over ranks), then its last result checked against the oracle."""
+    """GEMM + all-gather of C, three or four ways; each timed over the same
+    number of steps (max over ranks), then its last result checked against
+    the oracle."""
     import torch
     import torch.distributed as dist
 
     from infinite_dreams import dispatch, infinite_dreams_ext as ext
-    from infinite_dreams.sharded import release_peer_buffers, sharded_gemm
+    from infinite_dreams.sharded import MulticastUnavailable, multicast_supported, release_peer_buffers, sharded_gemm
 
     Cfull = torch.empty((size, N), device=dev, dtype=torch.float16)
     n_ag = max(1, min(args.steps, 20))
@@ -726,13 +730,33 @@ def time_exchange(args, A, B, C, step, cfg_id, size, rows, N, world, dev, stream
     ms_fused = timed(fused)
     check("fused_allgather", fused_out[0])
     fused_out.clear()
+
+    def multicast():
+        # every tile stored once through the multicast address of all ranks' C; NVSwitch writes the copies
+        fused_out[:] = [sharded_gemm(A, B, M_total=size, gather=True, exchange="multicast")]
+
+    ms_mc, mc_note = None, None
+    if N % 8 == 0 and multicast_supported(dev):
+        try:
+            ms_mc = timed(multicast)
+            check("multicast_allgather", fused_out[0])
+        except MulticastUnavailable as e:   # raised on every rank together
+            mc_note = f"unavailable: {e}"
+        fused_out.clear()
+    else:
+        mc_note = "unavailable: NVLink multicast is not supported on every rank's GPU" if N % 8 == 0 else \
+            "unavailable: N is not a multiple of 8"
     flop = 2.0 * size ** 3
     out = {"ms_per_step_gemm_then_allgather": ms_one, "value_gemm_then_allgather": flop / (ms_one * 1e-3) / 1e12,
            "ms_per_step_pipelined_2_chunks": ms_pipe, "value_pipelined": flop / (ms_pipe * 1e-3) / 1e12,
            "ms_per_step_fused": ms_fused, "value_fused": flop / (ms_fused * 1e-3) / 1e12,
+           "ms_per_step_multicast": ms_mc,
+           "value_multicast": flop / (ms_mc * 1e-3) / 1e12 if ms_mc else None,
+           "multicast": mc_note or "ran",
            "bytes_received_per_rank": (world - 1) * rows * N * 2, "steps": n_ag,
            "note": ("each rank ends every step with the whole 16384x16384 C; times are max over ranks. fused: the "
-                    "kernel's epilogue stores every tile into every rank's C over NVLink (TMA stores)")}
+                    "kernel's epilogue stores every tile into every rank's C over NVLink (TMA stores); multicast: "
+                    "it stores every tile once through an NVSwitch multicast address (multimem.st)")}
     del Cfull
     release_peer_buffers()
     return out

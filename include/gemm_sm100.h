@@ -144,6 +144,20 @@ int gemm_launch_gather(const void* A, const void* B, void* C, int64_t M, int64_t
                        int64_t ldb, int64_t ldc, const void* const* peer_C, int n_peers, int cfg_id,
                        void* workspace, size_t workspace_bytes, void* stream);
 
+/* Multicast all-gather: same as gemm_launch_gather, but every rank's full C
+ * is bound to one NVLink multicast object (NVLS) and C_mc is the multicast
+ * address of this rank's rows (C is their ordinary address on this GPU).
+ * Each finished box of C is stored once, through C_mc, and NVSwitch writes
+ * it into every rank's copy, this rank's included: the GPU sends each byte
+ * of C once instead of once per peer.  C_mc must come from a multicast
+ * mapping that covers M rows of pitch ldc; C and C_mc 16-byte aligned, N
+ * and ldc multiples of 8, tile_m >= 128 and split_k = 1
+ * (GEMM_ERR_UNSUPPORTED otherwise).  Completion across ranks as for
+ * gemm_launch_gather.  Extends the reference, which ran on one GPU. */
+int gemm_launch_multicast(const void* A, const void* B, void* C, void* C_mc, int64_t M, int64_t N, int64_t K,
+                          int64_t lda, int64_t ldb, int64_t ldc, int cfg_id, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
 /* CUDA IPC of device memory between the processes of one node, for
  * gemm_launch_gather.  gemm_ipc_export writes the GEMM_IPC_HANDLE_BYTES-byte
  * handle of the allocation that holds ptr and ptr's offset inside it;

@@ -266,6 +266,7 @@ struct OpDesc {
   int act = 0;
   const void* const* peers = nullptr;  // fused all-gather targets (gemm_launch_gather)
   int n_peers = 0;
+  void* mc_C = nullptr;  // multicast address of C's rows (gemm_launch_multicast)
   bool epi() const { return alpha != 1.0f || beta != 0.0f || bias != nullptr || act != 0; }
 };
 
@@ -533,7 +534,8 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
     p.peer_C[i] = i < op.n_peers ? static_cast<__half*>(const_cast<void*>(op.peers[i])) : nullptr;
   }
   std::memset(p.peer_map, 0, sizeof(p.peer_map));
-  if (op.n_peers > 0 && (pl.skinny || pl.max_parts > 1 || K == 0)) {
+  p.mc_C = static_cast<__half*>(op.mc_C);
+  if ((op.n_peers > 0 || op.mc_C) && (pl.skinny || pl.max_parts > 1 || K == 0)) {
     return fail(GEMM_ERR_UNSUPPORTED, "the fused all-gather needs K > 0 and a configuration without split-K / "
                                       "stream-K and with tile_m >= 128");
   }
@@ -650,7 +652,8 @@ int launch_impl(const void* A, const void* B, void* C, int64_t M, int64_t N, int
     st = encode_2d_cached(&tmB, b_src, N, K, b_ld, 64, kBK, "B");
   }
   if (st != GEMM_OK) return st;
-  const bool c_tma = tma_addressable(C, ldc);
+  // With a multicast C every box leaves through multimem stores instead.
+  const bool c_tma = !op.mc_C && tma_addressable(C, ldc);
   if (c_tma) {
     st = encode_2d_cached(&tmC, C, N, M, ldc, kStoreCols, kStoreRows, "C");
     if (st != GEMM_OK) return st;
@@ -792,6 +795,20 @@ int gemm_launch_gather(const void* A, const void* B, void* C, int64_t M, int64_t
   OpDesc op;
   op.peers = peer_C;
   op.n_peers = n_peers;
+  return launch_impl(A, B, C, M, N, K, lda, ldb, ldc, op, cfg_id, workspace, workspace_bytes, stream);
+}
+
+int gemm_launch_multicast(const void* A, const void* B, void* C, void* C_mc, int64_t M, int64_t N, int64_t K,
+                          int64_t lda, int64_t ldb, int64_t ldc, int cfg_id, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  t_last_error.clear();
+  if (!C_mc) return fail(GEMM_ERR_INVALID_ARG, "C_mc must be non-null");
+  if (reinterpret_cast<uintptr_t>(C_mc) % 16u || reinterpret_cast<uintptr_t>(C) % 16u || N % 8 || ldc % 8) {
+    return fail(GEMM_ERR_UNSUPPORTED, "the multicast all-gather needs 16-byte aligned C and C_mc and N and ldc "
+                                      "multiples of 8");
+  }
+  OpDesc op;
+  op.mc_C = C_mc;
   return launch_impl(A, B, C, M, N, K, lda, ldb, ldc, op, cfg_id, workspace, workspace_bytes, stream);
 }
 

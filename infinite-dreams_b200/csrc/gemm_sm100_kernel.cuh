@@ -97,6 +97,13 @@ struct GemmParams {
   int peer_tma;
   __half* peer_C[kMaxPeers];
   CUtensorMap peer_map[kMaxPeers];
+  // Multicast all-gather: mc_C is this rank's rows of C at an NVLink
+  // multicast address (same pitch ldc) of a C that every rank holds.  Each
+  // staged box is stored once, with multimem.st, and NVSwitch writes it into
+  // every rank's copy, this rank's included; C itself is then not written
+  // separately.  Non-split configs, N and ldc multiples of 8, c_tma = 0,
+  // n_peers = 0.
+  __half* mc_C;
 };
 
 template <int BN, int STAGES, int CG>
@@ -449,6 +456,25 @@ __device__ __forceinline__ void copy_box_to_peers(const GemmParams& p, const uin
         for (int e = 0; e < 8 && c + e < p.N; ++e) dst[e] = h[e];
       }
     }
+  }
+}
+
+// Stores one staged [32 x 64] box through the multicast address of C (every
+// rank's copy at once), with the same lane layout as copy_box_to_peers.  N
+// is a multiple of 8, so a lane's 8-column segment is wholly inside or
+// wholly outside C.
+__device__ __forceinline__ void store_box_multicast(const GemmParams& p, const uint8_t* buf, int row0, int col0,
+                                                    int lane) {
+  const int seg = lane & 7;
+  const int c = col0 + seg * 8;
+  if (c >= p.N) return;
+#pragma unroll 4
+  for (int i = 0; i < 8; ++i) {
+    const int r = 4 * i + (lane >> 3);
+    const int gr = row0 + r;
+    if (gr >= p.M) break;
+    const uint4 v = *reinterpret_cast<const uint4*>(buf + r * 128 + ((seg ^ (r & 7)) << 4));
+    multimem_st_v4(p.mc_C + static_cast<long long>(gr) * p.ldc + c, v);
   }
 }
 
@@ -910,6 +936,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
               }
               bulk_commit_group();
             }
+          } else if (p.mc_C) {
+            __syncwarp();  // every lane's row is staged
+            store_box_multicast(p, buf, row0, col0, lane);
+            __syncwarp();
           } else {
             __syncwarp();
             for (int r = 0; r < kStoreRows; ++r) {
@@ -966,9 +996,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         bulk_wait_group_read<0>();
       }
     }
-    // Peer stores are ordered before anything this thread does later (the
-    // grid's completion, which the ranks then agree on through NCCL).
-    if (p.n_peers > 0) {
+    // Peer and multicast stores are ordered before anything this thread does
+    // later (the grid's completion, which the ranks then agree on through NCCL).
+    if (p.n_peers > 0 || p.mc_C) {
       __syncwarp();
       __threadfence_system();
     }

@@ -210,6 +210,17 @@ __device__ __forceinline__ void bulk_wait_group() {
   asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// 16-byte store through an NVLink multicast (NVLS) address: NVSwitch writes
+// the value into the memory of every GPU bound to the multicast object, so
+// one store leaves this GPU once whatever the number of GPUs.  `mc` must be a
+// 16-byte aligned address inside a multicast mapping; the four words are
+// stored as raw bits (a store does no arithmetic on the .f32 type).
+__device__ __forceinline__ void multimem_st_v4(void* mc, uint4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
 // Make generic-proxy writes to shared memory visible to the async proxy
 // (TMA store / tcgen05.mma operand reads).
 __device__ __forceinline__ void fence_proxy_async_smem() {

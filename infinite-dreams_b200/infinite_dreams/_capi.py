@@ -53,6 +53,8 @@ _SIG = [
     ("gemm_launch_gather", ctypes.c_int,
      [_P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_int,
       _P, ctypes.c_size_t, _P]),
+    ("gemm_launch_multicast", ctypes.c_int,
+     [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, ctypes.c_int, _P, ctypes.c_size_t, _P]),
     ("gemm_ipc_export", ctypes.c_int, [_P, _P, ctypes.POINTER(ctypes.c_int64)]),
     ("gemm_ipc_import", ctypes.c_int, [_P, _I64, ctypes.POINTER(ctypes.c_void_p)]),
     ("gemm_ipc_close", ctypes.c_int, [_P]),

@@ -20,6 +20,15 @@ the remaining tiles' mainloop.  A one-element NCCL all-reduce issued after
 the launch on the same stream marks the point where every rank's grid, and
 with it every write into this rank's C, has completed.  No kernel reads
 another GPU's memory; peers are only written to.
+
+``exchange="multicast"`` is the same exchange through NVSwitch multicast
+(NVLS): every rank's full C is bound to one multicast object (torch's
+symmetric memory sets it up), and the kernel stores each finished box once,
+at its multicast address, with ``multimem.st``; the switch writes it into
+every rank's copy (``gemm_launch_multicast``).  Each GPU then sends its
+block of C once instead of once per peer, so at 8 ranks the GEMM's own SMs
+issue 1/7 of the outgoing stores.  It needs GPUs that support multicast
+(``multicast_supported``).
 """
 from __future__ import annotations
 
@@ -66,14 +75,17 @@ def sharded_gemm(A_local: torch.Tensor, B: torch.Tensor, M_total: Optional[int] 
     tile to all ranks from inside the GEMM; the returned full C is a buffer
     owned by this module: it stays intact until the second fused call of
     that shape after this one, provided whatever reads it is issued on the
-    calling stream before the next fused call.
+    calling stream before the next fused call.  ``exchange="multicast"``
+    does the same through one NVSwitch multicast store per box (N a
+    multiple of 8); it raises ``MulticastUnavailable`` on every rank when
+    some rank's GPU has no multicast.
     """
-    if exchange not in ("nccl", "fused"):
-        raise ValueError("exchange must be 'nccl' or 'fused'")
-    if exchange == "fused" and gather and dist.is_initialized() and dist.get_world_size(group) > 1:
+    if exchange not in ("nccl", "fused", "multicast"):
+        raise ValueError("exchange must be 'nccl', 'fused' or 'multicast'")
+    if exchange != "nccl" and gather and dist.is_initialized() and dist.get_world_size(group) > 1:
         if out is not None or compute is not None:
-            raise ValueError("exchange='fused' owns its output buffer and runs the kernel bank itself")
-        return _fused_gather(A_local, B, M_total, group)
+            raise ValueError(f"exchange='{exchange}' owns its output buffer and runs the kernel bank itself")
+        return _fused_gather(A_local, B, M_total, group, multicast=exchange == "multicast")
     compute = compute or _default_compute
     if gather and chunks > 1 and dist.is_initialized() and dist.get_world_size(group) > 1:
         full = _pipelined_gather(A_local, B, M_total, group, out, compute, chunks)
@@ -152,6 +164,33 @@ _ipc_lock = threading.Lock()
 # (rows, N, device, group key) -> two (full C buffer, [peer base pointer or None per rank]) pairs used
 # alternately, and the index of the next one
 _fused_buffers: Dict[Tuple[int, int, int, int], list] = {}
+# the same for the multicast exchange: two (full C buffer, multicast address of its first element,
+# symmetric-memory handle) triples used alternately, and the index of the next one
+_mc_buffers: Dict[Tuple[int, int, int, int], list] = {}
+
+
+class MulticastUnavailable(RuntimeError):
+    """Raised on every rank when some rank's GPU offers no NVLink multicast."""
+
+
+def _local_multicast(device: torch.device) -> bool:
+    """Whether this rank's GPU supports NVLink multicast."""
+    if device.type != "cuda":
+        return False
+    try:
+        from torch._C._distributed_c10d import _SymmetricMemory
+        from torch.distributed._symmetric_memory import DeviceType
+
+        return bool(_SymmetricMemory.has_multicast_support(DeviceType.CUDA, device.index))
+    except (ImportError, AttributeError, RuntimeError):
+        return False
+
+
+def multicast_supported(device: torch.device, group=None) -> bool:
+    """Whether every rank's GPU supports NVLink multicast (collective: every rank calls it)."""
+    flag = torch.tensor([int(_local_multicast(device))], dtype=torch.int32, device=device)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+    return bool(int(flag.item()))
 
 
 def _group_key(group) -> int:
@@ -219,6 +258,45 @@ def _share_buffer(rows: int, N: int, device: torch.device, group) -> Tuple[torch
     return full, peers
 
 
+def _mc_buffer(rows: int, N: int, device: torch.device, group) -> Tuple[torch.Tensor, int]:
+    """This rank's full C for the next multicast call and the multicast address of its first element.
+    Two buffers per shape, used in turn, for the reason given in ``_fused_buffer``; set up (collectively)
+    on the first call for a shape."""
+    key = (rows, N, device.index, _group_key(group))
+    with _ipc_lock:
+        entry = _mc_buffers.get(key)
+    if entry is None:
+        if not _equal_rows(rows, device, group):
+            raise ValueError("exchange='multicast' needs equal row blocks on every rank")
+        if not multicast_supported(device, group):
+            raise MulticastUnavailable("NVLink multicast is not supported on every rank's GPU")
+        entry = [_mc_share(rows, N, device, group), _mc_share(rows, N, device, group), 0]
+        with _ipc_lock:
+            _mc_buffers[key] = entry
+    full, mc, _ = entry[entry[2]]
+    entry[2] ^= 1
+    return full, mc
+
+
+def _mc_share(rows: int, N: int, device: torch.device, group) -> Tuple[torch.Tensor, int, object]:
+    """A new full-size C, bound with every other rank's to one multicast object (collective)."""
+    import torch.distributed._symmetric_memory as symm_mem
+
+    world = dist.get_world_size(group)
+    if symm_mem.get_backend(device) != "CUDA":
+        symm_mem.set_backend("CUDA")
+    full = symm_mem.empty((rows * world, N), dtype=torch.float16, device=device)
+    handle = symm_mem.rendezvous(full, group if group is not None else dist.group.WORLD)
+    mc = int(handle.multicast_ptr or 0)
+    off = full.data_ptr() - int(handle.buffer_ptrs[handle.rank])
+    good = int(mc != 0 and off >= 0 and off + full.numel() * 2 <= int(handle.buffer_size) and (mc + off) % 16 == 0)
+    flag = torch.tensor([good], dtype=torch.int32, device=device)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+    if not int(flag.item()):
+        raise MulticastUnavailable("the symmetric-memory rendezvous gave no multicast mapping of C on every rank")
+    return full, mc + off, handle
+
+
 def _gather_cfg(rows: int, N: int, K: int) -> int:
     """The dispatched config when the fused all-gather supports it (tile_m >= 128, no split-K), else a
     CTA-pair (or, for few rows, 1-CTA) tile without split."""
@@ -232,11 +310,13 @@ def _gather_cfg(rows: int, N: int, K: int) -> int:
     return _capi.cfg_find(fallback)
 
 
-def _fused_gather(A_local: torch.Tensor, B: torch.Tensor, M_total: Optional[int], group) -> torch.Tensor:
+def _fused_gather(A_local: torch.Tensor, B: torch.Tensor, M_total: Optional[int], group,
+                  multicast: bool = False) -> torch.Tensor:
     from . import _capi, infinite_dreams_ext as ext
 
+    name = "multicast" if multicast else "fused"
     if not (A_local.is_cuda and B.is_cuda):
-        raise ValueError("exchange='fused' needs CUDA tensors")
+        raise ValueError(f"exchange='{name}' needs CUDA tensors")
     ext._check_inputs(A_local, B)
     device = A_local.device
     rows, K = int(A_local.shape[0]), int(A_local.shape[1])
@@ -244,20 +324,31 @@ def _fused_gather(A_local: torch.Tensor, B: torch.Tensor, M_total: Optional[int]
     world, rank = dist.get_world_size(group), dist.get_rank(group)
     if M_total is not None and int(M_total) != rows * world:
         raise ValueError(f"row blocks sum to {rows * world}, expected {M_total}")
+    if multicast and N % 8:
+        raise ValueError("exchange='multicast' needs N to be a multiple of 8")
     A_local, B = A_local.contiguous(), B.contiguous()
-    full, peers = _fused_buffer(rows, N, device, group)   # raises on unequal row blocks
-    mine = full[rank * rows:(rank + 1) * rows]
     offset = rank * rows * N * 2
-    targets = [p + offset for p in peers if p is not None]
-    arr = (ctypes.c_void_p * max(len(targets), 1))(*targets)
+    # Both raise on unequal row blocks; the multicast one also when some rank has no multicast.
+    if multicast:
+        full, mc = _mc_buffer(rows, N, device, group)
+    else:
+        full, peers = _fused_buffer(rows, N, device, group)
+        targets = [p + offset for p in peers if p is not None]
+        arr = (ctypes.c_void_p * max(len(targets), 1))(*targets)
+    mine = full[rank * rows:(rank + 1) * rows]
     cid = _gather_cfg(rows, N, K)
     with torch.cuda.device(device):
         stream = torch.cuda.current_stream(device)
         need = _capi.lib.gemm_workspace_bytes(A_local.data_ptr(), B.data_ptr(), rows, N, K, K, N, cid)
         ws_ptr, ws_len = ext._workspace(device, stream, need) if need else (0, 0)
-        _capi.check(_capi.lib.gemm_launch_gather(A_local.data_ptr(), B.data_ptr(), mine.data_ptr(), rows, N, K, K, N,
-                                                 N, arr, len(targets), cid, ws_ptr or None, ws_len,
-                                                 stream.cuda_stream or None), "gemm_launch_gather")
+        if multicast:
+            _capi.check(_capi.lib.gemm_launch_multicast(A_local.data_ptr(), B.data_ptr(), mine.data_ptr(), mc + offset,
+                                                        rows, N, K, K, N, N, cid, ws_ptr or None, ws_len,
+                                                        stream.cuda_stream or None), "gemm_launch_multicast")
+        else:
+            _capi.check(_capi.lib.gemm_launch_gather(A_local.data_ptr(), B.data_ptr(), mine.data_ptr(), rows, N, K, K,
+                                                     N, N, arr, len(targets), cid, ws_ptr or None, ws_len,
+                                                     stream.cuda_stream or None), "gemm_launch_gather")
         # Ordered after this rank's grid on its stream: completes once every
         # rank's grid (and so every write into this rank's C) has finished.
         done = torch.zeros(1, dtype=torch.float32, device=device)
@@ -266,14 +357,24 @@ def _fused_gather(A_local: torch.Tensor, B: torch.Tensor, M_total: Optional[int]
 
 
 def release_peer_buffers(group=None) -> None:
-    """Unmaps the peers' buffers and drops the fused all-gather's own buffers.
+    """Unmaps the peers' buffers and drops the fused and multicast all-gathers' own buffers.
 
     Collective: every rank calls it (before destroying the process group), so
-    that no rank frees memory another rank still has mapped."""
+    that no rank frees memory another rank still has mapped, or leaves a
+    multicast object while another rank may still store through it."""
     from . import _capi
 
     with _ipc_lock:
         items = [(k, v) for k, v in _fused_buffers.items() if k[3] == _group_key(group)]
+        mc_keys = [k for k in _mc_buffers if k[3] == _group_key(group)]
+    if mc_keys:
+        torch.cuda.synchronize()
+        dist.barrier(group=group)   # no rank's kernel stores through a multicast address any more
+        with _ipc_lock:
+            for k in mc_keys:
+                _mc_buffers.pop(k, None)
+        torch.cuda.synchronize()
+        dist.barrier(group=group)   # every rank has dropped its buffers before any goes on
     if not items:
         return
     torch.cuda.synchronize()

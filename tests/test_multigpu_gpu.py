@@ -1,7 +1,8 @@
 """M-row sharding across GPUs with NCCL (skipped with fewer than 2 GPUs).
 
 Each rank computes its contiguous row block of C with the kernel bank; the
-optional all-gather (NCCL) assembles C, which must equal the oracle's."""
+optional all-gather -- NCCL, the fused NVLink stores, or the NVSwitch
+multicast stores -- assembles C, which must equal the oracle's."""
 import os
 import socket
 
@@ -31,7 +32,8 @@ def _worker(rank, world, port, M, N, K, q):
     import torch.distributed as dist
 
     from helpers import make_inputs
-    from infinite_dreams.sharded import broadcast_b, release_peer_buffers, row_block, sharded_gemm
+    from infinite_dreams.sharded import (MulticastUnavailable, broadcast_b, release_peer_buffers, row_block,
+                                         sharded_gemm)
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
@@ -55,12 +57,24 @@ def _worker(rank, world, port, M, N, K, q):
                 fused.append(F.cpu().numpy().view(np.uint16).copy())
                 F.fill_(float("nan"))   # the next call must rewrite every element
         else:
+            for ex in ("fused", "multicast"):
+                try:
+                    sharded_gemm(A_local, Bd, M_total=M, gather=True, exchange=ex)
+                    fused.append(f"{ex} accepted unequal blocks")
+                except ValueError:
+                    pass
+        # the same through one multicast store per box, when every GPU offers multicast
+        mc, mc_status = [], "ran"
+        if M % world == 0:
             try:
-                sharded_gemm(A_local, Bd, M_total=M, gather=True, exchange="fused")
-                fused.append("accepted unequal blocks")
-            except ValueError:
-                pass
-        q.put((rank, C.cpu().numpy().view(np.uint16), fused))
+                for _ in range(3):
+                    F = sharded_gemm(A_local, Bd, M_total=M, gather=True, exchange="multicast")
+                    torch.cuda.synchronize()
+                    mc.append(F.cpu().numpy().view(np.uint16).copy())
+                    F.fill_(float("nan"))
+            except MulticastUnavailable as e:
+                mc_status = f"unavailable: {e}"
+        q.put((rank, C.cpu().numpy().view(np.uint16), fused, mc, mc_status))
         release_peer_buffers()
         dist.barrier(device_ids=[rank])
     finally:
@@ -87,7 +101,8 @@ def test_sharded_gemm_nccl_allgather(cuda_device, M):
     A, B = make_inputs(M, N, K, seed=5)
     ref = oracle_gemm(A, B).astype(np.float32)
     tol = 1e-2 * np.sqrt(K / 1024) * np.abs(ref).max() + 1e-3
-    for rank, c, fused in results:
+    statuses = set()
+    for rank, c, fused, mc, mc_status in results:
         got = c.view(np.float16).astype(np.float32)
         assert got.shape == ref.shape
         assert np.abs(got - ref).max() <= tol, rank
@@ -97,6 +112,17 @@ def test_sharded_gemm_nccl_allgather(cuda_device, M):
             assert g.shape == ref.shape and np.isfinite(g).all(), rank
             assert np.abs(g - ref).max() <= tol, ("fused", rank)
         assert len(fused) == (3 if M % world == 0 else 0)
+        for f in mc:
+            g = f.view(np.float16).astype(np.float32)
+            assert g.shape == ref.shape and np.isfinite(g).all(), ("multicast", rank)
+            assert np.abs(g - ref).max() <= tol, ("multicast", rank)
+        statuses.add(mc_status)
+        if M % world == 0 and mc_status == "ran":
+            assert len(mc) == 3
+    assert len(statuses) == 1, statuses          # every rank ran it, or every rank was refused
+    if M % world == 0 and statuses != {"ran"}:
+        # NCCL and fused were checked above; say that this node left the multicast exchange out
+        pytest.skip(f"multicast exchange {statuses.pop()}")
 
 
 def _worker_large(rank, world, port, S, q):
@@ -113,7 +139,7 @@ def _worker_large(rank, world, port, S, q):
     import torch.distributed as dist
 
     import oracle
-    from infinite_dreams.sharded import broadcast_b, release_peer_buffers, sharded_gemm
+    from infinite_dreams.sharded import MulticastUnavailable, broadcast_b, release_peer_buffers, sharded_gemm
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
@@ -135,6 +161,10 @@ def _worker_large(rank, world, port, S, q):
         A_local = block(rank)
         C = sharded_gemm(A_local, Bd, M_total=S, gather=True)
         F = sharded_gemm(A_local, Bd, M_total=S, gather=True, exchange="fused")
+        try:
+            Mc = sharded_gemm(A_local, Bd, M_total=S, gather=True, exchange="multicast")
+        except MulticastUnavailable:
+            Mc = None
         torch.cuda.synchronize()
 
         # first, last and two inner rows of every rank's block
@@ -148,8 +178,12 @@ def _worker_large(rank, world, port, S, q):
         got_f = F[picks].float().cpu().numpy()
         err_c = float(np.abs(got_c - ref).max()) if np.isfinite(got_c).all() else float("inf")
         err_f = float(np.abs(got_f - ref).max()) if np.isfinite(got_f).all() else float("inf")
-        q.put((rank, err_c, err_f, tol))
-        del F
+        err_m = None
+        if Mc is not None:
+            got_m = Mc[picks].float().cpu().numpy()
+            err_m = float(np.abs(got_m - ref).max()) if np.isfinite(got_m).all() else float("inf")
+        q.put((rank, err_c, err_f, err_m, tol))
+        del F, Mc
         release_peer_buffers()
         dist.barrier(device_ids=[rank])
     finally:
@@ -158,7 +192,8 @@ def _worker_large(rank, world, port, S, q):
 
 def test_sharded_16384_cubed_sampled_rows(cuda_device):
     """The bench workload (16384^3, A row-sharded over every GPU, B replicated): the NCCL all-gather, the
-    fused exchange both give every rank a C whose sampled rows match the oracle."""
+    fused exchange and (where the GPUs offer multicast) the multicast exchange each give every rank a C
+    whose sampled rows match the oracle."""
     world = min(torch.cuda.device_count(), 8)
     if world < 2:
         pytest.skip("needs 2 or more GPUs")
@@ -172,6 +207,8 @@ def test_sharded_16384_cubed_sampled_rows(cuda_device):
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    for rank, err_c, err_f, tol in results:
+    for rank, err_c, err_f, err_m, tol in results:
         assert err_c <= tol, ("nccl all-gather", rank, err_c, tol)
         assert err_f <= tol, ("fused exchange", rank, err_f, tol)
+        assert err_m is None or err_m <= tol, ("multicast exchange", rank, err_m, tol)
+    assert len({r[3] is None for r in results}) == 1   # every rank ran it or every rank was refused
