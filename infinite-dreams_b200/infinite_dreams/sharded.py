@@ -283,17 +283,24 @@ def _mc_share(rows: int, N: int, device: torch.device, group) -> Tuple[torch.Ten
     import torch.distributed._symmetric_memory as symm_mem
 
     world = dist.get_world_size(group)
-    if symm_mem.get_backend(device) != "CUDA":
-        symm_mem.set_backend("CUDA")
-    full = symm_mem.empty((rows * world, N), dtype=torch.float16, device=device)
-    handle = symm_mem.rendezvous(full, group if group is not None else dist.group.WORLD)
-    mc = int(handle.multicast_ptr or 0)
-    off = full.data_ptr() - int(handle.buffer_ptrs[handle.rank])
-    good = int(mc != 0 and off >= 0 and off + full.numel() * 2 <= int(handle.buffer_size) and (mc + off) % 16 == 0)
+    good, why = 0, "no multicast mapping of C"
+    try:
+        if symm_mem.get_backend(device) != "CUDA":
+            symm_mem.set_backend("CUDA")
+        full = symm_mem.empty((rows * world, N), dtype=torch.float16, device=device)
+        handle = symm_mem.rendezvous(full, group if group is not None else dist.group.WORLD)
+        mc = int(handle.multicast_ptr or 0)
+        off = full.data_ptr() - int(handle.buffer_ptrs[handle.rank])
+        good = int(mc != 0 and off >= 0 and off + full.numel() * 2 <= int(handle.buffer_size)
+                   and (mc + off) % 16 == 0)
+    except RuntimeError as e:   # e.g. the multicast object could not be created; every rank agrees below
+        why = f"symmetric-memory set-up failed: {e}"
     flag = torch.tensor([good], dtype=torch.int32, device=device)
     dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
     if not int(flag.item()):
-        raise MulticastUnavailable("the symmetric-memory rendezvous gave no multicast mapping of C on every rank")
+        raise MulticastUnavailable(f"the symmetric-memory rendezvous gave no usable multicast mapping of C on every "
+                                   f"rank ({why} on this one)" if not good else
+                                   "another rank got no usable multicast mapping of C")
     return full, mc + off, handle
 
 

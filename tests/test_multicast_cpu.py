@@ -209,3 +209,15 @@ def test_two_ranks_agree_on_multicast_support():
 
 def test_local_multicast_is_false_off_gpu():
     assert sharded._local_multicast(torch.device("cpu")) is False
+
+
+def test_mc_share_setup_error_becomes_unavailable(mc_world, monkeypatch):
+    _fake_symm(monkeypatch, mc=0x1000)
+    import torch.distributed._symmetric_memory as symm_mem
+
+    def fail(t, group):
+        raise RuntimeError("multicast object could not be created")
+
+    monkeypatch.setattr(symm_mem, "rendezvous", fail)
+    with pytest.raises(sharded.MulticastUnavailable, match="could not be created"):
+        sharded._mc_share(32, 64, torch.device("cpu"), None)
