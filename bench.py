@@ -754,6 +754,8 @@ def time_exchange(args, A, B, C, step, cfg_id, size, rows, N, world, dev, stream
            "value_multicast": flop / (ms_mc * 1e-3) / 1e12 if ms_mc else None,
            "multicast": mc_note or "ran",
            "bytes_received_per_rank": (world - 1) * rows * N * 2, "steps": n_ag,
+           "best": min([("gemm_then_allgather", ms_one), ("pipelined_2_chunks", ms_pipe), ("fused", ms_fused)] +
+                       ([("multicast", ms_mc)] if ms_mc else []), key=lambda kv: kv[1])[0],
            "note": ("each rank ends every step with the whole 16384x16384 C; times are max over ranks. fused: the "
                     "kernel's epilogue stores every tile into every rank's C over NVLink (TMA stores); multicast: "
                     "it stores every tile once through an NVSwitch multicast address (multimem.st)")}
